@@ -1,0 +1,406 @@
+#!/usr/bin/env python
+"""MoE-layer benchmark (BASELINE.json metric: MoE-layer tokens/s, HBM GB/s at decode).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload ...]
+
+N = 1  -> BASELINE config 1: full-shape decode layer (H=4096, 512 experts top-10 + shared
+          expert, I=1024) on 64 tokens with uniform random router logits.
+N > 1  -> BASELINE config 3 (launched by torchrun, one rank per GPU): the same layer at TP=N
+          with the expert intermediate sharded (column-parallel gate_up, row-parallel down),
+          256 tokens, per-rank partial [256,4096] bf16 summed by one NCCL all-reduce.
+--workload prefill -> BASELINE config 2 on one GPU (8192 tokens, router GEMM on cuBLAS).
+
+Synthetic seeded data, random-init weights of the full shape.  Timed region: K steps between
+barrier + synchronize, CUDA events on the launching stream, max over ranks.  Every step
+streams >= 4.6 GB of expert weights, far more than the 126 MB L2, so no flush is needed.
+Prints one JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+METRIC = "MoE-layer tokens/s"
+H, E, K_TOP, INTER, SHARED = 4096, 512, 10, 1024, 1024
+STAGES = ["router_topk", "dispatch", "gather_quant", "gemm_gate_up", "gemm_down", "combine"]
+
+
+def peaks():
+    for path in (os.path.join(ROOT, "MEASURED_PEAKS.json"),):
+        if os.path.exists(path):
+            d = json.load(open(path))
+            return float(d["hbm_gbs"]), float(d.get("bf16_tflops", 1590.0)), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi samples (SM clock, throttle reasons) during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def setup_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        from muserve_b200 import distributed as D
+        D.init_distributed(backend="nccl", timeout_s=120)
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def max_over_ranks(x: float) -> float:
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+    return x
+
+
+def barrier():
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        dist.barrier()
+
+
+def expert_bytes(inter: int) -> int:
+    w = 3 * H * inter
+    s = ((2 * inter // 128) * (H // 128) + (H // 128) * (inter // 128)) * 4
+    return w + s
+
+
+def kernel_bytes(stage: str, n_touched: int, rows: int, inter: int, shared: int, tokens: int) -> int:
+    """Algorithmic HBM bytes of one launch: weights + scales of each touched expert (and the
+    shared expert) plus the activations the kernel must read and write once."""
+    kb_h, kb_i = H // 128, inter // 128
+    if stage == "gemm_gate_up":
+        w = (n_touched + (1 if shared else 0)) * (2 * inter * H + 2 * kb_i * kb_h * 4)
+        return w + rows * (H + kb_h * 4) + rows * (inter + kb_i * 4)
+    if stage == "gemm_down":
+        w = (n_touched + (1 if shared else 0)) * (H * inter + kb_h * kb_i * 4)
+        return w + rows * (inter + kb_i * 4) + rows * H * 2
+    raise ValueError(stage)
+
+
+def layer_bytes(n_touched, inter, shared, tokens):
+    return (n_touched + (1 if shared else 0)) * expert_bytes(inter) + 2 * tokens * H * 2
+
+
+def traffic_for(workload: str, kernel: str):
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(path):
+        d = json.load(open(path))
+        return d.get(workload, {}).get(kernel)
+    return None
+
+
+def run_ours(args, world, rank, local):
+    import ctypes
+
+    from muserve_b200 import _lib, moe, synthetic
+    from muserve_b200.loader import shard_moe_weights
+    lib = _lib.load()
+    dev = torch.device("cuda", local)
+    prefill = args.workload == "prefill"
+    tokens = args.tokens or (8192 if prefill else (64 if world == 1 else 256))
+    tp = world
+    # weights: the full layer from one seed on every rank, then this rank's intermediate shard
+    w = synthetic.make_layer_weights(H, E, INTER, SHARED, seed=1, device=dev)
+    if tp > 1:
+        w = shard_moe_weights(w, tp, rank, "inter")
+        torch.cuda.empty_cache()
+    inter = w["moe.experts.gate_proj.weight"].shape[1]
+    shared = w["moe.shared_expert.gate_proj.weight"].shape[0]
+    x = synthetic.make_hidden(tokens, H, seed=2, device=dev)
+    if prefill:
+        logits = torch.nn.functional.linear(x, w["moe.gate.weight"]).float().contiguous()
+    else:
+        logits = synthetic.uniform_logits(tokens, E, seed=3, device=dev)
+    ws_struct, info = moe.weights_struct(w)
+    shape = _lib.MoeShape(tokens=tokens, hidden=H, num_experts=E, top_k=K_TOP, inter=inter, shared_inter=shared,
+                          placement=0, tp=1, rank=0, add_shared=1, combine_mode=_lib.COMBINE_V2,
+                          weights_dtype=_lib.MSV_BF16)
+    nbytes = lib.msv_moe_forward_workspace_size(ctypes.byref(shape))
+    wsbuf = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    out = torch.empty(tokens, H, dtype=torch.bfloat16, device=dev)
+    tw = torch.empty(tokens, K_TOP, dtype=torch.bfloat16, device=dev)
+    tid = torch.empty(tokens, K_TOP, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    nst = len(STAGES) + 1
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(nst)] for _ in range(args.steps)]
+    ar_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for row in evs:  # create the event handles before anything is timed
+        for e in row:
+            e.record(stream)
+    ev_arrays = [(ctypes.c_void_p * nst)(*[e.cuda_event for e in row]) for row in evs]
+
+    def step(i=None):
+        if i is not None:
+            arr = ev_arrays[i]
+            rc = lib.msv_moe_forward_profiled(ctypes.byref(shape), ctypes.byref(ws_struct), x.data_ptr(),
+                                              logits.data_ptr(), tw.data_ptr(), tid.data_ptr(), out.data_ptr(), 0,
+                                              wsbuf.data_ptr(), nbytes, sp, arr)
+        else:
+            rc = lib.msv_moe_forward(ctypes.byref(shape), ctypes.byref(ws_struct), x.data_ptr(), logits.data_ptr(),
+                                     tw.data_ptr(), tid.data_ptr(), out.data_ptr(), 0, wsbuf.data_ptr(), nbytes, sp)
+        _lib.check(rc, "msv_moe_forward")
+        if tp > 1:
+            if i is not None:
+                ar_ev[i][0].record(stream)
+            dist.all_reduce(out)
+            if i is not None:
+                ar_ev[i][1].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    _lib.check(lib.msv_check_device_error(sp), "warmup")
+    # routing statistics of the measured step (identical every step)
+    counts = torch.bincount(tid.flatten().long(), minlength=E)
+    n_touched = int((counts > 0).sum().item())
+    rows = tokens * K_TOP + tokens
+    barrier()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        t0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        t1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms_total = max_over_ranks(t0.elapsed_time(t1))
+    _lib.check(lib.msv_check_device_error(sp), "timed region")
+    stage_ms = {s: statistics.mean(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(args.steps))
+                for j, s in enumerate(STAGES)}
+    ar_ms = statistics.mean(a.elapsed_time(b) for a, b in ar_ev) if tp > 1 else 0.0
+    ms_step = ms_total / args.steps
+    value = tokens * args.steps / (ms_total / 1e3)
+    hbm, _, peak_kind = peaks()
+    dom = max(("gemm_gate_up", "gemm_down"), key=lambda s: stage_ms[s])
+    dom_bytes = kernel_bytes(dom, n_touched, rows, inter, shared, tokens)
+    achieved = dom_bytes / (stage_ms[dom] / 1e3) / 1e9
+    layer_gbs = layer_bytes(n_touched, inter, shared, tokens) / (ms_step / 1e3) / 1e9
+    flops = 6 * H * inter * tokens * K_TOP + 6 * H * shared * tokens
+    workload = ("prefill_c2" if prefill else "decode_c1") if tp == 1 else f"tp{tp}_decode_c3"
+
+    # e2e: through the reference-facing API from pinned host buffers, result read back each step
+    e2e = None
+    if not args.no_e2e:
+        from muserve_b200 import moe as M
+        hx = x.cpu().pin_memory()
+        hl = logits.cpu().pin_memory()
+        ho = torch.empty(tokens, H, dtype=torch.bfloat16).pin_memory()
+        dx = torch.empty_like(x)
+        dl = torch.empty_like(logits)
+
+        def e2e_step():
+            dx.copy_(hx, non_blocking=True)
+            dl.copy_(hl, non_blocking=True)
+            o = M.moe_layer(dx, w, top_k=K_TOP, num_experts=E, router_logits=dl)
+            if tp > 1:
+                dist.all_reduce(o)
+            ho.copy_(o, non_blocking=True)
+        for _ in range(args.warmup):
+            e2e_step()
+        barrier()
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        a1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ms_e2e = max_over_ranks(a0.elapsed_time(a1))
+        e2e = {"value": tokens * args.steps / (ms_e2e / 1e3), "unit": "tokens/s",
+               "h2d_bytes_per_step": hx.numel() * 2 + hl.numel() * 4, "d2h_bytes_per_step": ho.numel() * 2,
+               "ms_per_step": ms_e2e / args.steps}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(x, logits, w, tokens=min(tokens, 64) if not prefill else 16)
+    res = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "e4m3 x e4m3 -> fp32 acc, bf16 io",
+        "data": "synthetic (seeded N(0,1) hidden, N(0,0.02) block-quantised weights, " +
+                ("router GEMM logits)" if prefill else "uniform random router logits)"),
+        "config": {"workload": workload, "tokens": tokens, "hidden": H, "experts": E, "top_k": K_TOP,
+                   "inter_per_rank": inter, "shared_inter_per_rank": shared, "tp": tp,
+                   "parallelism": f"tp{tp}" if tp > 1 else "single",
+                   "l2": f"no flush: each step streams {layer_bytes(n_touched, inter, shared, tokens) / 1e9:.2f} GB"
+                         " of expert weights (> 126 MB L2)"},
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "peak_kind": peak_kind,
+                     "traffic": traffic_for(workload, dom), "algorithmic_bytes_per_launch": dom_bytes},
+        "layer": {"hbm_gbs": layer_gbs, "hbm_frac": layer_gbs / hbm, "n_touched_experts": n_touched,
+                  "fp8_tflops": flops / (ms_step / 1e3) / 1e12, "stage_ms": stage_ms,
+                  "allreduce_ms": ar_ms, "allreduce_share": ar_ms / ms_step if tp > 1 else 0.0},
+        "gpu_launches": 6 * args.steps,
+        "clocks": clk.summary(),
+        "e2e": e2e,
+        "cpu_baseline": cpu,
+    }
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+
+
+def cpu_baseline(x, logits, w, tokens):
+    """The reference's algorithm on the host cores (the CPU oracle port, all threads), on
+    ``tokens`` tokens of the same workload with their GPU routing.  Only the touched routed
+    experts are copied to the host."""
+    from oracle import moe_oracle as orc
+    torch.set_num_threads(os.cpu_count())
+    xs = x[:tokens].cpu()
+    tw, tid = orc.route(logits[:tokens].cpu(), K_TOP)
+    shared = {k: v.cpu() for k, v in w.items() if k.startswith("moe.shared")}
+    experts = sorted(set(tid.flatten().tolist()))
+    cache = {}
+    for e in experts:
+        cache[e] = (torch.cat([w["moe.experts.gate_proj.weight"][e], w["moe.experts.up_proj.weight"][e]]).cpu(),
+                    torch.cat([w["moe.experts.gate_proj.weight_scale_inv"][e],
+                               w["moe.experts.up_proj.weight_scale_inv"][e]]).cpu(),
+                    w["moe.experts.down_proj.weight"][e].cpu(), w["moe.experts.down_proj.weight_scale_inv"][e].cpu())
+    t = time.perf_counter()
+    orc.moe_forward_tokens(xs, shared, tw, tid, expert_fn=lambda e: cache[e])
+    dt = time.perf_counter() - t
+    return {"value": tokens / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{tokens} tokens of the same layer ({len(experts)} experts touched), one pass, "
+                      f"{dt:.1f} s"}
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the reference's algorithm (CPU oracle port; the reference itself is
+    MUSA-only and not installable here) on the box's host cores, same metric and config."""
+    if rank != 0:
+        return
+    from muserve_b200 import synthetic
+    from oracle import moe_oracle as orc
+    torch.set_num_threads(os.cpu_count())
+    dev = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
+    tokens = 64
+    x = synthetic.make_hidden(tokens, H, seed=2, device=dev).cpu()
+    logits = synthetic.uniform_logits(tokens, E, seed=3, device=dev).cpu()
+    tw, tid = orc.route(logits, K_TOP)
+    per_step = 8  # bounded sample per step: 8 of the 64 tokens (cycling), ~75 experts
+    g = torch.Generator().manual_seed(1)
+    cache = {}
+
+    def fetch(e):
+        if e not in cache:
+            gen = torch.Generator().manual_seed(1000 + e)
+            gq, gs = orc.quantize_weight_blockwise(torch.randn(2 * INTER, H, generator=gen) * 0.02)
+            dq, ds = orc.quantize_weight_blockwise(torch.randn(H, INTER, generator=gen) * 0.02)
+            cache[e] = (gq, gs, dq, ds)
+        return cache[e]
+    shared = {}
+    for name, shp in (("gate_proj", (SHARED, H)), ("up_proj", (SHARED, H)), ("down_proj", (H, SHARED))):
+        q, s = orc.quantize_weight_blockwise(torch.randn(*shp, generator=g) * 0.02)
+        shared[f"moe.shared_expert.{name}.weight"] = q
+        shared[f"moe.shared_expert.{name}.weight_scale_inv"] = s
+    shared["moe.shared_expert_gate.weight"] = (torch.randn(1, H, generator=g) * 0.02).to(torch.bfloat16)
+    for e in sorted(set(tid.flatten().tolist())):  # weight preparation is not timed
+        fetch(e)
+
+    def step(i):
+        sl = slice((i * per_step) % tokens, (i * per_step) % tokens + per_step)
+        orc.moe_forward_tokens(x[sl], shared, tw[sl], tid[sl], expert_fn=fetch)
+    for i in range(args.warmup):
+        step(i)
+    t = time.perf_counter()
+    for i in range(args.steps):
+        step(i)
+    dt = time.perf_counter() - t
+    value = per_step * args.steps / dt
+    sample = f"{per_step} of 64 tokens per step (cycling), full layer math, torch CPU, {os.cpu_count()} threads"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 dequantised to fp32 (torch CPU)",
+        "data": "synthetic (seeded)", "config": {"workload": "decode_c1", "tokens": tokens, "hidden": H, "experts": E,
+                                                 "top_k": K_TOP, "inter_per_rank": INTER, "tp": 1},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"])
+    ap.add_argument("--tokens", type=int, default=0)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, world, rank)
+        return
+    world, rank, local = setup_dist()
+    try:
+        run_ours(args, world, rank, local)
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,664 @@
+// Host side of the C ABI declared in include/muserve_moe.h: argument checks, tensor-map
+// cache, kernel-variant choice and the launch sequence of the MoE layer.  Nothing here
+// allocates device memory or synchronises a stream (msv_check_device_error excepted).
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+
+#include "common.cuh"
+#include "grouped_gemm.cuh"
+#include "quant_combine.cuh"
+#include "route.cuh"
+
+namespace msv {
+
+// Error word raised by device-side bounded waits (MSV_ERR_TIMEOUT); one per device.
+__device__ int g_dev_err;
+
+namespace {
+
+thread_local std::string t_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_err = buf;
+  return code;
+}
+
+int cuda_check(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return MSV_OK;
+  return fail(MSV_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+struct DeviceInfo {
+  int num_sms = 0;
+  int* err_word = nullptr;
+};
+
+std::mutex g_mu;
+DeviceInfo g_dev[64];
+
+int device_info(DeviceInfo** out) {
+  int dev = 0;
+  if (int rc = cuda_check(cudaGetDevice(&dev), "cudaGetDevice")) return rc;
+  if (dev < 0 || dev >= 64) return fail(MSV_ERR_UNSUPPORTED, "device index %d", dev);
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (d.num_sms == 0) {
+    int major = 0;
+    if (int rc = cuda_check(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev), "attr"))
+      return rc;
+    if (major != 10) return fail(MSV_ERR_UNSUPPORTED, "device %d is sm_%d0; this library is built for sm_100a", dev, major);
+    if (int rc = cuda_check(cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev), "attr"))
+      return rc;
+    void* p = nullptr;
+    if (int rc = cuda_check(cudaGetSymbolAddress(&p, g_dev_err), "cudaGetSymbolAddress(g_dev_err)")) return rc;
+    d.err_word = static_cast<int*>(p);
+  }
+  *out = &d;
+  return MSV_OK;
+}
+
+// ── tensor maps ───────────────────────────────────────────────────────────────────────────
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+struct MapKey {
+  uintptr_t base;
+  uint64_t rows, cols, stride;
+  uint32_t box_rows;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && rows == o.rows && cols == o.cols && stride == o.stride && box_rows == o.box_rows;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    size_t h = k.base * 0x9E3779B97F4A7C15ull;
+    h ^= (k.rows + 0x632BE59BD9B4E019ull) + (h << 6) + (h >> 2);
+    h ^= (k.cols * 31 + k.stride * 131 + k.box_rows) + (h << 6) + (h >> 2);
+    return h;
+  }
+};
+std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
+
+// 2-D e4m3 (byte) matrix [rows, cols] with row stride `stride` bytes, box [box_rows x 128 B],
+// 128-byte swizzle, zero fill out of bounds.  Cached: a map only encodes addresses and sizes.
+int tensor_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t cols, uint64_t stride, uint32_t box_rows) {
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return fail(MSV_ERR_INVALID, "operand not 16-byte aligned");
+  if (stride % 16 != 0 || cols % 128 != 0) return fail(MSV_ERR_INVALID, "operand row stride / width not multiple of 16/128");
+  MapKey key{reinterpret_cast<uintptr_t>(base), rows, cols, stride, box_rows};
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_maps.find(key);
+    if (it != g_maps.end()) {
+      *out = it->second;
+      return MSV_OK;
+    }
+  }
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(MSV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {stride};
+  cuuint32_t box[2] = {128, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MSV_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d) rows=%llu cols=%llu", (int)r,
+                                     (unsigned long long)rows, (unsigned long long)cols);
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_maps.size() > 8192) g_maps.clear();
+  g_maps.emplace(key, m);
+  *out = m;
+  return MSV_OK;
+}
+
+// ── grouped GEMM variants ────────────────────────────────────────────────────────────────
+
+using G1Small = GemmCfg<32, 2, 1, 1>;   // gate+up -> SwiGLU -> e4m3, <= 32 rows per chunk
+using G1Large = GemmCfg<128, 2, 1, 4>;  // same, <= 128 rows per chunk
+using G2Small = GemmCfg<32, 1, 0, 1>;   // plain -> bf16, <= 32 rows per chunk
+using G2Large = GemmCfg<256, 1, 0, 4>;  // plain -> bf16, <= 256 rows per chunk
+
+template <class C>
+int launch_gemm(const GemmArgs& a, cudaStream_t st, int num_sms) {
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!configured[dev]) {
+    if (int rc = cuda_check(cudaFuncSetAttribute(k_grouped_gemm<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 C::SMEM_BYTES),
+                            "cudaFuncSetAttribute(grouped_gemm)"))
+      return rc;
+    configured[dev] = true;
+  }
+  k_grouped_gemm<C><<<num_sms, C::THREADS, C::SMEM_BYTES, st>>>(a);
+  return cuda_check(cudaGetLastError(), "launch grouped_gemm");
+}
+
+int launch_gemm_variant(int epi, bool small, const GemmArgs& a, cudaStream_t st, int nsm) {
+  if (epi == 1) return small ? launch_gemm<G1Small>(a, st, nsm) : launch_gemm<G1Large>(a, st, nsm);
+  return small ? launch_gemm<G2Small>(a, st, nsm) : launch_gemm<G2Large>(a, st, nsm);
+}
+int variant_bn(int epi, bool small) {
+  if (epi == 1) return small ? G1Small::BN : G1Large::BN;
+  return small ? G2Small::BN : G2Large::BN;
+}
+
+// ── workspace carving ────────────────────────────────────────────────────────────────────
+
+struct Carver {
+  uint8_t* base;
+  size_t off = 0;
+  template <class T>
+  T* take(size_t count) {
+    off = (off + 255) & ~size_t(255);
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += count * sizeof(T);
+    return p;
+  }
+};
+
+size_t tile_cap(int groups, int rows, int bn, int nb) {
+  return (size_t)nb * ((size_t)groups + (size_t)(rows + bn - 1) / bn + 1);
+}
+
+bool is_pow2_aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+}  // namespace
+}  // namespace msv
+
+using namespace msv;
+
+// ═════════════════════════════════════════════════════════════════════════════════════════
+extern "C" {
+
+const char* msv_last_error(void) { return t_err.c_str(); }
+int msv_version(void) { return 100; }
+
+int msv_check_device_error(msv_stream_t stream) {
+  DeviceInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  if (int rc = cuda_check(cudaStreamSynchronize(stream), "cudaStreamSynchronize")) return rc;
+  int v = 0;
+  if (int rc = cuda_check(cudaMemcpy(&v, d->err_word, sizeof(int), cudaMemcpyDeviceToHost), "read error word")) return rc;
+  int z = 0;
+  if (int rc = cuda_check(cudaMemcpy(d->err_word, &z, sizeof(int), cudaMemcpyHostToDevice), "clear error word")) return rc;
+  if (v != 0) return fail(MSV_ERR_TIMEOUT, "a bounded device-side wait gave up (code %d)", v);
+  return MSV_OK;
+}
+
+int msv_route_topk(const float* logits, int64_t ld, int T, int E, int k, int renormalize, void* topk_w, int w_dtype,
+                   void* topk_ids, int ids_dtype, msv_stream_t stream) {
+  if (!logits || !topk_ids || T < 0 || E < 1 || E > 1024 || k < 1 || k > 16 || k > E || ld < E)
+    return fail(MSV_ERR_INVALID, "msv_route_topk: bad arguments (T=%d E=%d k=%d ld=%lld)", T, E, k, (long long)ld);
+  if ((w_dtype != MSV_F32 && w_dtype != MSV_BF16) || (ids_dtype != MSV_I32 && ids_dtype != MSV_I64))
+    return fail(MSV_ERR_INVALID, "msv_route_topk: dtype codes");
+  if (T == 0) return MSV_OK;
+  const size_t sm = route_smem_bytes(E);
+  k_route_topk<<<(T + kRouteWarps - 1) / kRouteWarps, kRouteWarps * 32, sm, stream>>>(
+      logits, ld, T, E, k, 1, renormalize, topk_w, w_dtype, topk_ids, ids_dtype, nullptr);
+  return cuda_check(cudaGetLastError(), "launch route_topk");
+}
+
+int msv_topk_select(const float* values, int64_t ld, int T, int E, int k, void* topk_ids, int ids_dtype,
+                    float* out_values, msv_stream_t stream) {
+  if (!values || !topk_ids || T < 0 || E < 1 || E > 1024 || k < 1 || k > 16 || k > E || ld < E)
+    return fail(MSV_ERR_INVALID, "msv_topk_select: bad arguments");
+  if (ids_dtype != MSV_I32 && ids_dtype != MSV_I64) return fail(MSV_ERR_INVALID, "msv_topk_select: ids dtype");
+  if (T == 0) return MSV_OK;
+  k_route_topk<<<(T + kRouteWarps - 1) / kRouteWarps, kRouteWarps * 32, route_smem_bytes(E), stream>>>(
+      values, ld, T, E, k, 0, 0, nullptr, MSV_F32, topk_ids, ids_dtype, out_values);
+  return cuda_check(cudaGetLastError(), "launch topk_select");
+}
+
+int msv_moe_permute(const void* topk_ids, int ids_dtype, int T, int k, int num_experts, int placement, int tp, int rank,
+                    int alignment, int64_t* sort_order, int64_t* inverse_order, int32_t* sorted_expert_ids,
+                    int32_t* expert_counts, int32_t* num_local, msv_stream_t stream) {
+  if (!topk_ids || !num_local || T < 0 || k < 1 || num_experts < 1 || (ids_dtype != MSV_I32 && ids_dtype != MSV_I64))
+    return fail(MSV_ERR_INVALID, "msv_moe_permute: bad arguments");
+  if (placement && (tp < 1 || rank < 0 || rank >= tp)) return fail(MSV_ERR_INVALID, "msv_moe_permute: tp/rank");
+  const int e_local = placement ? (num_experts + tp - 1) / tp : num_experts;
+  if (e_local > 1024) return fail(MSV_ERR_UNSUPPORTED, "msv_moe_permute: more than 1024 local experts");
+  PermuteArgs p{};
+  p.ids = topk_ids;
+  p.ids_i64 = ids_dtype == MSV_I64;
+  p.T = T;
+  p.k = k;
+  p.num_experts = num_experts;
+  p.placement = placement;
+  p.tp = placement ? tp : 1;
+  p.rank = placement ? rank : 0;
+  p.alignment = alignment;
+  p.e_local = e_local;
+  p.sort_order = sort_order;
+  p.inverse_order = inverse_order;
+  p.sorted_expert_ids = sorted_expert_ids;
+  p.expert_counts = expert_counts;
+  p.num_local = num_local;
+  const size_t sm = permute_smem_bytes(e_local);
+  if (sm > 48 * 1024)
+    if (int rc = cuda_check(cudaFuncSetAttribute(k_permute, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
+                            "cudaFuncSetAttribute(permute)"))
+      return rc;
+  k_permute<<<1, kPermThreads, sm, stream>>>(p);
+  return cuda_check(cudaGetLastError(), "launch permute");
+}
+
+int msv_fp8_quant_128(const void* x, int64_t ldx, int M, int K, const int32_t* row_index, uint8_t* q, int64_t ldq,
+                      float* scale, int64_t s_row, int64_t s_kb, msv_stream_t stream) {
+  if (!x || !q || !scale || M < 0 || K <= 0 || K % 128 != 0 || ldx < K || ldq < K)
+    return fail(MSV_ERR_INVALID, "msv_fp8_quant_128: bad arguments (M=%d K=%d)", M, K);
+  if (!is_pow2_aligned(x, 16) || (ldx * 2) % 16 != 0 || !is_pow2_aligned(q, 8) || ldq % 8 != 0)
+    return fail(MSV_ERR_INVALID, "msv_fp8_quant_128: x rows must be 16-byte aligned, q rows 8-byte aligned");
+  if (M == 0) return MSV_OK;
+  QuantArgs a{};
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.ldx = ldx;
+  a.K = K;
+  a.rows_a = M;
+  a.idx_a = row_index;
+  a.q = q;
+  a.ldq = ldq;
+  a.scale = scale;
+  a.s_row = s_row;
+  a.s_kb = s_kb;
+  k_quant_rows<<<(M + kQuantWarps - 1) / kQuantWarps, kQuantWarps * 32, 0, stream>>>(a);
+  return cuda_check(cudaGetLastError(), "launch quant");
+}
+
+size_t msv_ragged_gemm_workspace_size(int M, int N) {
+  Carver c{nullptr};
+  c.take<int4>(tile_cap(M, M, 32, N / 128));
+  c.take<int>(1);
+  return c.off + 256;
+}
+
+int msv_ragged_moe_gemm_fp8(const uint8_t* a, const float* a_scale, int M, int K, const uint8_t* w, const float* w_scale,
+                            int E, int N, const int32_t* m_indices, void* out, void* workspace, size_t ws_bytes,
+                            msv_stream_t stream) {
+  if (!a || !a_scale || !w || !w_scale || !m_indices || !out || M < 0 || K <= 0 || N <= 0 || E <= 0 ||
+      K % 128 != 0 || N % 128 != 0)
+    return fail(MSV_ERR_INVALID, "msv_ragged_moe_gemm_fp8: bad arguments (M=%d K=%d N=%d E=%d)", M, K, N, E);
+  if (M == 0) return MSV_OK;
+  if (!workspace || ws_bytes < msv_ragged_gemm_workspace_size(M, N) || !is_pow2_aligned(workspace, 256))
+    return fail(MSV_ERR_INVALID, "msv_ragged_moe_gemm_fp8: workspace too small or not 256-byte aligned");
+  DeviceInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  const bool small = (M / E) <= 24;
+  const int bn = variant_bn(0, small), nb = N / 128;
+  const size_t cap = tile_cap(M, M, 32, nb);
+  Carver c{static_cast<uint8_t*>(workspace)};
+  int4* tiles = c.take<int4>(cap);
+  int* ntiles = c.take<int>(1);
+  k_tiles_from_runs<<<1, 1024, 0, stream>>>(m_indices, M, bn, nb, tiles, ntiles, (int)cap);
+  if (int rc = cuda_check(cudaGetLastError(), "launch tiles_from_runs")) return rc;
+  GemmArgs g{};
+  if (int rc = tensor_map(&g.tmA[0][0], w, (uint64_t)E * N, K, K, 128)) return rc;
+  g.tmA[1][0] = g.tmA[0][0];
+  if (int rc = tensor_map(&g.tmB, a, M, K, K, bn)) return rc;
+  g.a_expert_rows[0] = g.a_expert_rows[1] = N;
+  g.ws[0][0] = g.ws[1][0] = w_scale;
+  g.ws[0][1] = g.ws[1][1] = w_scale;
+  g.ws_expert_stride[0] = g.ws_expert_stride[1] = (int64_t)(N / 128) * (K / 128);
+  g.ws_nb_stride = K / 128;
+  g.as = a_scale;
+  g.as_row = K / 128;
+  g.as_kb = 1;
+  g.tiles = tiles;
+  g.num_tiles = ntiles;
+  g.num_kb = K / 128;
+  g.out = out;
+  g.out_ld = N;
+  g.err = d->err_word;
+  return launch_gemm_variant(0, small, g, stream, d->num_sms);
+}
+
+size_t msv_gemm_fp8_workspace_size(int M, int N) {
+  Carver c{nullptr};
+  c.take<int4>(tile_cap(1, M, 32, N / 128));
+  c.take<int>(1);
+  return c.off + 256;
+}
+
+int msv_gemm_fp8_nt_groupwise(const uint8_t* a, const float* a_scale, int M, int K, const uint8_t* b,
+                              const float* b_scale, int N, void* out, void* workspace, size_t ws_bytes,
+                              msv_stream_t stream) {
+  if (!a || !a_scale || !b || !b_scale || !out || M < 0 || K <= 0 || N <= 0 || K % 128 != 0 || N % 128 != 0)
+    return fail(MSV_ERR_INVALID, "msv_gemm_fp8_nt_groupwise: bad arguments (M=%d K=%d N=%d)", M, K, N);
+  if (M == 0) return MSV_OK;
+  if (!workspace || ws_bytes < msv_gemm_fp8_workspace_size(M, N) || !is_pow2_aligned(workspace, 256))
+    return fail(MSV_ERR_INVALID, "msv_gemm_fp8_nt_groupwise: workspace too small or not 256-byte aligned");
+  DeviceInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  const bool small = M <= 32;
+  const int bn = variant_bn(0, small), nb = N / 128;
+  Carver c{static_cast<uint8_t*>(workspace)};
+  int4* tiles = c.take<int4>(tile_cap(1, M, 32, nb));
+  int* ntiles = c.take<int>(1);
+  k_tiles_dense<<<64, 256, 0, stream>>>(M, bn, nb, tiles, ntiles);
+  if (int rc = cuda_check(cudaGetLastError(), "launch tiles_dense")) return rc;
+  GemmArgs g{};
+  if (int rc = tensor_map(&g.tmA[0][0], b, N, K, K, 128)) return rc;
+  g.tmA[1][0] = g.tmA[0][0];
+  if (int rc = tensor_map(&g.tmB, a, M, K, K, bn)) return rc;
+  g.a_expert_rows[0] = g.a_expert_rows[1] = 0;
+  g.ws[0][0] = g.ws[1][0] = g.ws[0][1] = g.ws[1][1] = b_scale;
+  g.ws_expert_stride[0] = g.ws_expert_stride[1] = 0;
+  g.ws_nb_stride = K / 128;
+  g.as = a_scale;
+  g.as_row = K / 128;
+  g.as_kb = 1;
+  g.tiles = tiles;
+  g.num_tiles = ntiles;
+  g.num_kb = K / 128;
+  g.out = out;
+  g.out_ld = N;
+  g.err = d->err_word;
+  return launch_gemm_variant(0, small, g, stream, d->num_sms);
+}
+
+// ── whole layer ──────────────────────────────────────────────────────────────────────────
+
+namespace {
+struct LayerPlan {
+  int T, H, E, k, I, Is, P, rows, e_local;
+  bool shared, small1, small2;
+  int bn1, bn2, nb1, nb2;
+  size_t cap1, cap2;
+};
+
+int plan_layer(const msv_moe_shape* s, LayerPlan* L) {
+  if (!s) return fail(MSV_ERR_INVALID, "msv_moe_forward: null shape");
+  L->T = s->tokens;
+  L->H = s->hidden;
+  L->E = s->num_experts;
+  L->k = s->top_k;
+  L->I = s->inter;
+  L->Is = s->shared_inter;
+  if (L->T < 0 || L->H <= 0 || L->H % 128 || L->E <= 0 || L->k < 1 || L->k > 16 || L->k > L->E || L->I <= 0 ||
+      L->I % 128 || L->Is < 0 || L->Is % 128)
+    return fail(MSV_ERR_INVALID, "msv_moe_forward: bad shape (T=%d H=%d E=%d k=%d I=%d Is=%d)", L->T, L->H, L->E,
+                L->k, L->I, L->Is);
+  if (s->placement && (s->tp < 1 || s->rank < 0 || s->rank >= s->tp || L->E % s->tp))
+    return fail(MSV_ERR_INVALID, "msv_moe_forward: placement 1 needs E %% tp == 0 and 0 <= rank < tp");
+  L->shared = L->Is > 0;
+  if (L->shared && L->Is != L->I)
+    return fail(MSV_ERR_UNSUPPORTED, "msv_moe_forward: shared intermediate (%d) must equal routed (%d)", L->Is, L->I);
+  L->e_local = s->placement ? L->E / s->tp : L->E;
+  if (L->e_local > 1024) return fail(MSV_ERR_UNSUPPORTED, "msv_moe_forward: more than 1024 local experts");
+  L->P = L->T * L->k;
+  L->rows = L->P + (L->shared ? L->T : 0);
+  const double avg = (double)L->P / (s->placement ? (double)s->tp : 1.0) / (double)L->e_local;
+  L->small1 = avg <= 24.0;
+  L->small2 = avg <= 24.0;
+  L->bn1 = variant_bn(1, L->small1);
+  L->bn2 = variant_bn(0, L->small2);
+  L->nb1 = L->I / 128;
+  L->nb2 = L->H / 128;
+  L->cap1 = tile_cap(L->e_local, L->P, L->bn1, L->nb1) + (size_t)L->nb1 * ((L->T + L->bn1 - 1) / L->bn1 + 1);
+  L->cap2 = tile_cap(L->e_local, L->P, L->bn2, L->nb2) + (size_t)L->nb2 * ((L->T + L->bn2 - 1) / L->bn2 + 1);
+  return MSV_OK;
+}
+
+struct LayerWs {
+  int32_t *ids, *counts, *num_local, *slot_row, *row_token;
+  void* w;
+  int4 *tiles1, *tiles2;
+  int *ntiles1, *ntiles2;
+  uint8_t *xq, *aq;
+  float *xs, *as, *gate_val;
+  __nv_bfloat16* down;
+};
+
+size_t carve_layer(const LayerPlan& L, uint8_t* base, LayerWs* w) {
+  Carver c{base};
+  w->ids = c.take<int32_t>(L.P);
+  w->w = c.take<float>(L.P);
+  w->counts = c.take<int32_t>(L.e_local);
+  w->num_local = c.take<int32_t>(1);
+  w->slot_row = c.take<int32_t>(L.P);
+  w->row_token = c.take<int32_t>(L.P);
+  w->tiles1 = c.take<int4>(L.cap1);
+  w->ntiles1 = c.take<int>(1);
+  w->tiles2 = c.take<int4>(L.cap2);
+  w->ntiles2 = c.take<int>(1);
+  w->xq = c.take<uint8_t>((size_t)L.rows * L.H);
+  w->xs = c.take<float>((size_t)L.rows * (L.H / 128));
+  w->aq = c.take<uint8_t>((size_t)L.rows * L.I);
+  w->as = c.take<float>((size_t)L.rows * (L.I / 128));
+  w->down = c.take<__nv_bfloat16>((size_t)L.rows * L.H);
+  w->gate_val = c.take<float>((size_t)(L.T > 0 ? L.T : 1));
+  return c.off + 256;
+}
+}  // namespace
+
+size_t msv_moe_forward_workspace_size(const msv_moe_shape* shape) {
+  LayerPlan L;
+  if (plan_layer(shape, &L) != MSV_OK) return 0;
+  LayerWs w;
+  return carve_layer(L, nullptr, &w);
+}
+
+namespace {
+int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const void* hidden, const float* logits,
+                     void* topk_w, int32_t* topk_ids, void* out, int flags, void* workspace, size_t ws_bytes,
+                     cudaStream_t stream, cudaEvent_t* ev) {
+  auto mark = [&](int i) -> int {
+    return ev ? cuda_check(cudaEventRecord(ev[i], stream), "cudaEventRecord") : (int)MSV_OK;
+  };
+  LayerPlan L;
+  if (int rc = plan_layer(s, &L)) return rc;
+  if (!W || !hidden || !out) return fail(MSV_ERR_INVALID, "msv_moe_forward: null weights/hidden/out");
+  const bool given = flags & MSV_FWD_ROUTING_GIVEN;
+  if (given && (!topk_w || !topk_ids)) return fail(MSV_ERR_INVALID, "msv_moe_forward: routing given but null");
+  if (!given && !logits) return fail(MSV_ERR_INVALID, "msv_moe_forward: null router logits");
+  if (!W->gate_w || !W->up_w || !W->gate_s || !W->up_s || !W->down_w || !W->down_s)
+    return fail(MSV_ERR_INVALID, "msv_moe_forward: null routed-expert weight");
+  if (L.shared && (!W->sh_gate_w || !W->sh_up_w || !W->sh_down_w || !W->sh_gate_s || !W->sh_up_s || !W->sh_down_s))
+    return fail(MSV_ERR_INVALID, "msv_moe_forward: null shared-expert weight");
+  if (s->weights_dtype != MSV_BF16 && s->weights_dtype != MSV_F32)
+    return fail(MSV_ERR_INVALID, "msv_moe_forward: weights_dtype");
+  if (s->combine_mode < 0 || s->combine_mode > 2) return fail(MSV_ERR_INVALID, "msv_moe_forward: combine_mode");
+  if (!is_pow2_aligned(hidden, 16) || !is_pow2_aligned(out, 16))
+    return fail(MSV_ERR_INVALID, "msv_moe_forward: hidden/out must be 16-byte aligned");
+  if (L.T == 0) return MSV_OK;
+  LayerWs w;
+  const size_t need = carve_layer(L, nullptr, &w);
+  if (!workspace || ws_bytes < need || !is_pow2_aligned(workspace, 256))
+    return fail(MSV_ERR_INVALID, "msv_moe_forward: workspace %zu < %zu bytes or not 256-byte aligned", ws_bytes, need);
+  carve_layer(L, static_cast<uint8_t*>(workspace), &w);
+  DeviceInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+
+  // 1. router
+  int32_t* ids = topk_ids ? topk_ids : w.ids;
+  void* rw = topk_w ? topk_w : w.w;
+  if (int rc = mark(0)) return rc;
+  if (!given) {
+    k_route_topk<<<(L.T + kRouteWarps - 1) / kRouteWarps, kRouteWarps * 32, route_smem_bytes(L.E), stream>>>(
+        logits, L.E, L.T, L.E, L.k, 1, 1, rw, s->weights_dtype, ids, MSV_I32, nullptr);
+    if (int rc = cuda_check(cudaGetLastError(), "launch route_topk")) return rc;
+  }
+  // 2. dispatch bookkeeping + tile lists
+  PermuteArgs p{};
+  p.ids = ids;
+  p.ids_i64 = 0;
+  p.T = L.T;
+  p.k = L.k;
+  p.num_experts = L.E;
+  p.placement = s->placement;
+  p.tp = s->placement ? s->tp : 1;
+  p.rank = s->placement ? s->rank : 0;
+  p.alignment = 0;
+  p.e_local = L.e_local;
+  p.expert_counts = w.counts;
+  p.num_local = w.num_local;
+  p.row_token = w.row_token;
+  p.slot_row = w.slot_row;
+  p.tiles1 = w.tiles1;
+  p.ntiles1 = w.ntiles1;
+  p.bn1 = L.bn1;
+  p.nb1 = L.nb1;
+  p.tiles2 = w.tiles2;
+  p.ntiles2 = w.ntiles2;
+  p.bn2 = L.bn2;
+  p.nb2 = L.nb2;
+  const bool do_shared = L.shared && s->add_shared;  // ranks that do not add it skip its GEMMs
+  p.shared_rows = do_shared ? L.T : 0;
+  p.row_base_shared = L.P;
+  const size_t psm = permute_smem_bytes(L.e_local);
+  if (psm > 48 * 1024)
+    if (int rc = cuda_check(cudaFuncSetAttribute(k_permute, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psm),
+                            "cudaFuncSetAttribute(permute)"))
+      return rc;
+  if (int rc = mark(1)) return rc;
+  k_permute<<<1, kPermThreads, psm, stream>>>(p);
+  if (int rc = cuda_check(cudaGetLastError(), "launch permute")) return rc;
+  if (int rc = mark(2)) return rc;
+  // 3. gather + quantise (routed rows in expert order, then the shared expert's rows)
+  QuantArgs q{};
+  q.x = static_cast<const __nv_bfloat16*>(hidden);
+  q.ldx = L.H;
+  q.K = L.H;
+  q.rows_a = L.P;
+  q.idx_a = w.row_token;
+  q.nvalid_a = w.num_local;
+  q.rows_b = do_shared ? L.T : 0;
+  q.q = w.xq;
+  q.ldq = L.H;
+  q.scale = w.xs;
+  q.s_row = 1;
+  q.s_kb = L.rows;
+  q.gate_w = (do_shared && W->sh_gate_logit_w) ? static_cast<const __nv_bfloat16*>(W->sh_gate_logit_w) : nullptr;
+  q.gate_val = w.gate_val;
+  k_quant_rows<<<(L.rows + kQuantWarps - 1) / kQuantWarps, kQuantWarps * 32, 0, stream>>>(q);
+  if (int rc = cuda_check(cudaGetLastError(), "launch quant")) return rc;
+  if (int rc = mark(3)) return rc;
+  // 4. gate_up GEMM with SwiGLU + requant epilogue
+  GemmArgs g1{};
+  const uint64_t gu_rows = (uint64_t)(L.e_local - 1) * W->gu_expert_rows + L.I;
+  if (int rc = tensor_map(&g1.tmA[0][0], W->gate_w, gu_rows, L.H, L.H, 128)) return rc;
+  if (int rc = tensor_map(&g1.tmA[0][1], W->up_w, gu_rows, L.H, L.H, 128)) return rc;
+  if (L.shared) {
+    if (int rc = tensor_map(&g1.tmA[1][0], W->sh_gate_w, L.Is, L.H, L.H, 128)) return rc;
+    if (int rc = tensor_map(&g1.tmA[1][1], W->sh_up_w, L.Is, L.H, L.H, 128)) return rc;
+  } else {
+    g1.tmA[1][0] = g1.tmA[0][0];
+    g1.tmA[1][1] = g1.tmA[0][1];
+  }
+  if (int rc = tensor_map(&g1.tmB, w.xq, L.rows, L.H, L.H, L.bn1)) return rc;
+  g1.a_expert_rows[0] = (int)W->gu_expert_rows;
+  g1.a_expert_rows[1] = 0;
+  g1.ws[0][0] = W->gate_s;
+  g1.ws[0][1] = W->up_s;
+  g1.ws[1][0] = L.shared ? W->sh_gate_s : W->gate_s;
+  g1.ws[1][1] = L.shared ? W->sh_up_s : W->up_s;
+  g1.ws_expert_stride[0] = W->gu_scale_expert_stride;
+  g1.ws_expert_stride[1] = 0;
+  g1.ws_nb_stride = L.H / 128;
+  g1.as = w.xs;
+  g1.as_row = 1;
+  g1.as_kb = L.rows;
+  g1.tiles = w.tiles1;
+  g1.num_tiles = w.ntiles1;
+  g1.num_kb = L.H / 128;
+  g1.out = w.aq;
+  g1.out_ld = L.I;
+  g1.out_scale = w.as;
+  g1.os_row = 1;
+  g1.os_kb = L.rows;
+  g1.err = d->err_word;
+  if (int rc = launch_gemm_variant(1, L.small1, g1, stream, d->num_sms)) return rc;
+  if (int rc = mark(4)) return rc;
+  // 5. down GEMM
+  GemmArgs g2{};
+  if (int rc = tensor_map(&g2.tmA[0][0], W->down_w, (uint64_t)L.e_local * L.H, L.I, L.I, 128)) return rc;
+  if (L.shared) {
+    if (int rc = tensor_map(&g2.tmA[1][0], W->sh_down_w, L.H, L.Is, L.Is, 128)) return rc;
+  } else {
+    g2.tmA[1][0] = g2.tmA[0][0];
+  }
+  g2.tmA[0][1] = g2.tmA[0][0];
+  g2.tmA[1][1] = g2.tmA[1][0];
+  if (int rc = tensor_map(&g2.tmB, w.aq, L.rows, L.I, L.I, L.bn2)) return rc;
+  g2.a_expert_rows[0] = L.H;
+  g2.a_expert_rows[1] = 0;
+  g2.ws[0][0] = g2.ws[0][1] = W->down_s;
+  g2.ws[1][0] = g2.ws[1][1] = L.shared ? W->sh_down_s : W->down_s;
+  g2.ws_expert_stride[0] = (int64_t)(L.H / 128) * (L.I / 128);
+  g2.ws_expert_stride[1] = 0;
+  g2.ws_nb_stride = L.I / 128;
+  g2.as = w.as;
+  g2.as_row = 1;
+  g2.as_kb = L.rows;
+  g2.tiles = w.tiles2;
+  g2.num_tiles = w.ntiles2;
+  g2.num_kb = L.I / 128;
+  g2.out = w.down;
+  g2.out_ld = L.H;
+  g2.err = d->err_word;
+  if (int rc = launch_gemm_variant(0, L.small2, g2, stream, d->num_sms)) return rc;
+  if (int rc = mark(5)) return rc;
+  // 6. weighted combine (+ shared expert)
+  CombineArgs cb{};
+  cb.down = w.down;
+  cb.ld_down = L.H;
+  cb.slot_row = w.slot_row;
+  cb.topk_ids = ids;
+  cb.topk_w = rw;
+  cb.w_f32 = s->weights_dtype == MSV_F32;
+  cb.T = L.T;
+  cb.H = L.H;
+  cb.k = L.k;
+  cb.mode = s->combine_mode;
+  cb.add_shared = do_shared;
+  cb.shared_row0 = L.P;
+  cb.gate_val = (do_shared && W->sh_gate_logit_w) ? w.gate_val : nullptr;
+  cb.out = static_cast<__nv_bfloat16*>(out);
+  cb.ld_out = L.H;
+  k_combine<<<L.T, kCombineThreads, 0, stream>>>(cb);
+  if (int rc = cuda_check(cudaGetLastError(), "launch combine")) return rc;
+  return mark(6);
+}
+}  // namespace
+
+int msv_moe_forward(const msv_moe_shape* s, const msv_moe_weights* W, const void* hidden, const float* logits,
+                    void* topk_w, int32_t* topk_ids, void* out, int flags, void* workspace, size_t ws_bytes,
+                    msv_stream_t stream) {
+  return moe_forward_impl(s, W, hidden, logits, topk_w, topk_ids, out, flags, workspace, ws_bytes, stream, nullptr);
+}
+
+int msv_moe_forward_profiled(const msv_moe_shape* s, const msv_moe_weights* W, const void* hidden,
+                             const float* logits, void* topk_w, int32_t* topk_ids, void* out, int flags,
+                             void* workspace, size_t ws_bytes, msv_stream_t stream, void* const* events) {
+  if (!events) return fail(MSV_ERR_INVALID, "msv_moe_forward_profiled: null events");
+  cudaEvent_t ev[7];
+  for (int i = 0; i < 7; ++i) ev[i] = static_cast<cudaEvent_t>(events[i]);
+  return moe_forward_impl(s, W, hidden, logits, topk_w, topk_ids, out, flags, workspace, ws_bytes, stream, ev);
+}
+
+}  // extern "C"

@@ -1,0 +1,194 @@
+// Per-row per-128-channel e4m3 quantisation (with dispatch gather) and the weighted
+// combine.  References: muserve/model/qwen35_layer_v2.py:71-86 (_fast_fp8_quantize),
+// :649-673 (unsort, weighted sum, shared expert add), muserve/kernels/moe_dispatch.py:75-77,
+// muserve/kernels/batched_moe.py:153-158.
+#pragma once
+#include "common.cuh"
+
+namespace msv {
+
+struct QuantArgs {
+  const __nv_bfloat16* x;
+  int64_t ldx;
+  int K;
+  // segment A: rows [0, rows_a) read x row idx_a[r] (idx_a == nullptr: identity); rows at or
+  // beyond *nvalid_a (when given) are skipped
+  int rows_a;
+  const int32_t* idx_a;
+  const int32_t* nvalid_a;
+  // segment B: rows [rows_a, rows_a + rows_b) read x row (r - rows_a)
+  int rows_b;
+  uint8_t* q;
+  int64_t ldq;
+  float* scale;
+  int64_t s_row, s_kb;
+  // shared-expert gate: gv[t] = bf16(sigmoid(bf16(x[t] . wg))) for segment-B rows
+  const __nv_bfloat16* gate_w;
+  float* gate_val;
+};
+
+constexpr int kQuantWarps = 8;
+
+// One warp per output row; each lane owns 8 consecutive channels (16 bytes) of a 256-channel
+// slab, so a 128-channel block is 16 lanes and its amax is a 4-step xor shuffle.
+__global__ void __launch_bounds__(kQuantWarps * 32) k_quant_rows(QuantArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int r = blockIdx.x * kQuantWarps + (threadIdx.x >> 5);
+  if (r >= a.rows_a + a.rows_b) return;
+  int64_t src;
+  bool seg_b = r >= a.rows_a;
+  if (!seg_b) {
+    if (a.nvalid_a && r >= *a.nvalid_a) return;
+    src = a.idx_a ? a.idx_a[r] : r;
+    if (src < 0) return;
+  } else {
+    src = r - a.rows_a;
+  }
+  const __nv_bfloat16* xr = a.x + src * a.ldx;
+  uint8_t* qr = a.q + (int64_t)r * a.ldq;
+  float dot = 0.f;
+  const bool want_gate = seg_b && a.gate_w != nullptr;
+  for (int c0 = 0; c0 < a.K; c0 += 256) {
+    const int c = c0 + lane * 8;
+    float f[8];
+    uint4 raw = make_uint4(0, 0, 0, 0);
+    if (c < a.K) raw = *reinterpret_cast<const uint4*>(xr + c);
+    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw);
+    float am = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      f[i] = __bfloat162float(h[i]);
+      am = nanmax(am, fabsf(f[i]));
+    }
+    if (want_gate && c < a.K) {
+      uint4 wraw = *reinterpret_cast<const uint4*>(a.gate_w + c);
+      const __nv_bfloat16* wh = reinterpret_cast<const __nv_bfloat16*>(&wraw);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) dot = fmaf(f[i], __bfloat162float(wh[i]), dot);
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) am = nanmax(am, __shfl_xor_sync(0xffffffffu, am, o));
+    // s = clamp(amax, min=1e-12) / 448 (NaN propagates as in torch.clamp)
+    const float s = (am != am) ? am : __fdiv_rn(fmaxf(am, 1e-12f), 448.0f);
+    if (c < a.K) {
+      uint32_t packed[2];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float lo = clamp_pm(__fdiv_rn(f[2 * i], s), 448.0f);
+        float hi = clamp_pm(__fdiv_rn(f[2 * i + 1], s), 448.0f);
+        uint16_t pr = f32x2_to_e4m3x2(lo, hi);
+        if (i & 1) packed[i >> 1] |= (uint32_t)pr << 16;
+        else packed[i >> 1] = pr;
+      }
+      *reinterpret_cast<uint2*>(qr + c) = make_uint2(packed[0], packed[1]);
+      if ((lane & 15) == 0) a.scale[(int64_t)r * a.s_row + (int64_t)(c / 128) * a.s_kb] = s;
+    }
+  }
+  if (want_gate) {
+    dot = warp_sum(dot);
+    if (lane == 0) {
+      float lg = bf16_round(dot);
+      float sg = bf16_round(1.0f / (1.0f + expf(-lg)));
+      a.gate_val[src] = sg;
+    }
+  }
+}
+
+struct CombineArgs {
+  const __nv_bfloat16* down;  // [rows, H] expert outputs in sorted-row order
+  int64_t ld_down;
+  const int32_t* slot_row;    // [T*k] row of each slot, -1 when not on this rank
+  const int32_t* topk_ids;    // [T*k] (orders the DISPATCH / BATCHED modes)
+  const void* topk_w;         // [T*k] bf16 or f32
+  int w_f32;
+  int T, H, k;
+  int mode;                   // msv_combine_mode
+  // shared expert: row (shared_row0 + t) of `down`, times gate_val[t] when gate_val != nullptr
+  int add_shared;
+  int shared_row0;
+  const float* gate_val;
+  __nv_bfloat16* out;
+  int64_t ld_out;
+};
+
+constexpr int kCombineThreads = 256;
+
+// One CTA per token; each thread produces 8 consecutive channels per pass.
+__global__ void __launch_bounds__(kCombineThreads) k_combine(CombineArgs a) {
+  const int t = blockIdx.x;
+  __shared__ int s_row[16];
+  __shared__ float s_w[16];
+  if (threadIdx.x == 0) {
+    int rows[16], ids[16];
+    float ws[16];
+    int n = 0;
+    for (int j = 0; j < a.k; ++j) {
+      int r = a.slot_row[(int64_t)t * a.k + j];
+      float w = a.w_f32 ? reinterpret_cast<const float*>(a.topk_w)[(int64_t)t * a.k + j]
+                        : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.topk_w)[(int64_t)t * a.k + j]);
+      rows[n] = r;
+      ws[n] = w;
+      ids[n] = a.topk_ids ? a.topk_ids[(int64_t)t * a.k + j] : j;
+      ++n;
+    }
+    if (a.mode != MSV_COMBINE_V2) {  // expert-ascending order of the per-expert loops
+      for (int i = 1; i < n; ++i) {
+        int r = rows[i], id = ids[i];
+        float w = ws[i];
+        int j = i - 1;
+        while (j >= 0 && ids[j] > id) {
+          rows[j + 1] = rows[j];
+          ws[j + 1] = ws[j];
+          ids[j + 1] = ids[j];
+          --j;
+        }
+        rows[j + 1] = r;
+        ws[j + 1] = w;
+        ids[j + 1] = id;
+      }
+    }
+    for (int j = 0; j < n; ++j) {
+      s_row[j] = rows[j];
+      s_w[j] = ws[j];
+    }
+  }
+  __syncthreads();
+  const float gv = (a.add_shared && a.gate_val) ? a.gate_val[t] : 1.0f;
+  for (int c = threadIdx.x * 8; c < a.H; c += kCombineThreads * 8) {
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    for (int j = 0; j < a.k; ++j) {
+      const int r = s_row[j];
+      if (r < 0) continue;
+      const float w = s_w[j];
+      uint4 raw = *reinterpret_cast<const uint4*>(a.down + (int64_t)r * a.ld_down + c);
+      const __nv_bfloat16* d = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float dv = __bfloat162float(d[i]);
+        if (a.mode == MSV_COMBINE_V2) acc[i] += bf16_round(dv * w);
+        // fp32 product and fp32 add rounded separately (no FMA contraction), then bf16
+        else if (a.mode == MSV_COMBINE_DISPATCH) acc[i] = bf16_round(__fadd_rn(acc[i], __fmul_rn(dv, w)));
+        else acc[i] = bf16_round(acc[i] + bf16_round(dv * w));
+      }
+    }
+    if (a.add_shared) {
+      uint4 raw = *reinterpret_cast<const uint4*>(a.down + (int64_t)(a.shared_row0 + t) * a.ld_down + c);
+      const __nv_bfloat16* d = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float sd = __bfloat162float(d[i]);
+        if (a.gate_val) sd = bf16_round(sd * gv);
+        acc[i] = bf16_round(bf16_round(acc[i]) + sd);
+      }
+    }
+    uint4 o;
+    __nv_bfloat16* oh = reinterpret_cast<__nv_bfloat16*>(&o);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) oh[i] = __float2bfloat16_rn(acc[i]);
+    *reinterpret_cast<uint4*>(a.out + (int64_t)t * a.ld_out + c) = o;
+  }
+}
+
+}  // namespace msv

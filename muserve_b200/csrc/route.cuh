@@ -1,0 +1,568 @@
+// Router (softmax + top-k + renormalise) and dispatch bookkeeping (stable counting sort by
+// local expert).  Reference: muserve/model/qwen35_layer_v2.py:568-605.
+//
+// Top-k order.  torch's CPU topk (the reference oracle) calls libstdc++
+//   std::nth_element(q, q+k-1, q+E, greater) ; std::sort(q, q+k-1, greater)   when k*64 >  E
+//   std::partial_sort(q, q+k, q+E, greater)                                   when k*64 <= E
+// over (value, index) pairs compared by value only, so the order of tied values is an
+// artefact of those algorithms (it is neither "lowest index first" nor stable).  The kernel
+// below replays both algorithms step for step: libstdc++'s introselect (median-of-three
+// pivot, unguarded Hoare partition, insertion sort below 4 elements, heap-select fallback
+// when the depth budget runs out) and its heap routines.  The partition, the only O(E) step,
+// runs warp-parallel: the left scan stops at every element !(x > p), the right scan at every
+// element !(p > x); the m-th left stop swaps with the m-th right stop while it lies to the
+// left of it, and the cut is min(next left stop, last swapped right stop).  That reproduces
+// the sequential scan exactly (both scans only ever read positions the other has not
+// swapped yet).  Comparisons use the logits: softmax is monotone, so the scores order and tie
+// exactly like the logits except where two distinct logits round to the same fp32 score.
+#pragma once
+#include "common.cuh"
+
+namespace msv {
+
+// comparator of torch's CPU topk for largest=true: NaN sorts first
+MSV_DEVICE bool gt(float x, float y) { return (x != x && y == y) || x > y; }
+
+struct Arr {
+  float* v;
+  uint16_t* ix;
+  MSV_DEVICE void swap(int a, int b) {
+    float tv = v[a];
+    v[a] = v[b];
+    v[b] = tv;
+    uint16_t ti = ix[a];
+    ix[a] = ix[b];
+    ix[b] = ti;
+  }
+};
+
+// ---- sequential libstdc++ pieces (run by one lane) ----------------------------------------
+
+MSV_DEVICE void insertion_sort(Arr a, int f, int l) {
+  if (f == l) return;
+  for (int i = f + 1; i < l; ++i) {
+    float val = a.v[i];
+    uint16_t vix = a.ix[i];
+    if (gt(val, a.v[f])) {
+      for (int j = i; j > f; --j) {
+        a.v[j] = a.v[j - 1];
+        a.ix[j] = a.ix[j - 1];
+      }
+      a.v[f] = val;
+      a.ix[f] = vix;
+    } else {
+      int j = i, n = i - 1;
+      while (gt(val, a.v[n])) {
+        a.v[j] = a.v[n];
+        a.ix[j] = a.ix[n];
+        j = n;
+        --n;
+      }
+      a.v[j] = val;
+      a.ix[j] = vix;
+    }
+  }
+}
+
+MSV_DEVICE void move_median_to_first(Arr a, int r, int x, int y, int z) {
+  if (gt(a.v[x], a.v[y])) {
+    if (gt(a.v[y], a.v[z])) a.swap(r, y);
+    else if (gt(a.v[x], a.v[z])) a.swap(r, z);
+    else a.swap(r, x);
+  } else if (gt(a.v[x], a.v[z])) a.swap(r, x);
+  else if (gt(a.v[y], a.v[z])) a.swap(r, z);
+  else a.swap(r, y);
+}
+
+MSV_DEVICE void push_heap(Arr a, int base, int hole, int top, float val, uint16_t vix) {
+  int parent = (hole - 1) / 2;
+  while (hole > top && gt(a.v[base + parent], val)) {
+    a.v[base + hole] = a.v[base + parent];
+    a.ix[base + hole] = a.ix[base + parent];
+    hole = parent;
+    parent = (hole - 1) / 2;
+  }
+  a.v[base + hole] = val;
+  a.ix[base + hole] = vix;
+}
+
+MSV_DEVICE void adjust_heap(Arr a, int base, int hole, int len, float val, uint16_t vix) {
+  const int top = hole;
+  int sc = hole;
+  while (sc < (len - 1) / 2) {
+    sc = 2 * (sc + 1);
+    if (gt(a.v[base + sc], a.v[base + sc - 1])) sc--;
+    a.v[base + hole] = a.v[base + sc];
+    a.ix[base + hole] = a.ix[base + sc];
+    hole = sc;
+  }
+  if ((len & 1) == 0 && sc == (len - 2) / 2) {
+    sc = 2 * (sc + 1);
+    a.v[base + hole] = a.v[base + sc - 1];
+    a.ix[base + hole] = a.ix[base + sc - 1];
+    hole = sc - 1;
+  }
+  push_heap(a, base, hole, top, val, vix);
+}
+
+MSV_DEVICE void make_heap(Arr a, int f, int l) {
+  const int len = l - f;
+  if (len < 2) return;
+  int parent = (len - 2) / 2;
+  while (true) {
+    adjust_heap(a, f, parent, len, a.v[f + parent], a.ix[f + parent]);
+    if (parent == 0) return;
+    parent--;
+  }
+}
+
+MSV_DEVICE void pop_heap(Arr a, int f, int l, int r) {
+  float val = a.v[r];
+  uint16_t vix = a.ix[r];
+  a.v[r] = a.v[f];
+  a.ix[r] = a.ix[f];
+  adjust_heap(a, f, 0, l - f, val, vix);
+}
+
+MSV_DEVICE void heap_select(Arr a, int f, int m, int l) {
+  make_heap(a, f, m);
+  for (int i = m; i < l; ++i)
+    if (gt(a.v[i], a.v[f])) pop_heap(a, f, m, i);
+}
+
+MSV_DEVICE void sort_heap(Arr a, int f, int l) {
+  while (l - f > 1) {
+    --l;
+    pop_heap(a, f, l, l);
+  }
+}
+
+// ---- warp-parallel unguarded partition of [lo, hi), pivot value p stored at lo-1 ---------
+
+MSV_DEVICE int warp_partition(Arr a, int lo, int hi, float p, uint16_t* lpos, uint16_t* rpos) {
+  const int lane = threadIdx.x & 31;
+  // compact left stops (ascending) and right stops (descending)
+  int nl = 0, nr = 0;
+  for (int base = lo; base < hi; base += 32) {
+    int i = base + lane;
+    bool stop = (i < hi) && !gt(a.v[i], p);
+    uint32_t bal = __ballot_sync(0xffffffffu, stop);
+    if (stop) lpos[nl + __popc(bal & lanemask_lt())] = (uint16_t)i;
+    nl += __popc(bal);
+  }
+  for (int base = hi - 1; base >= lo - 1; base -= 32) {
+    int j = base - lane;
+    bool stop = (j >= lo - 1) && !gt(p, a.v[j]);
+    uint32_t bal = __ballot_sync(0xffffffffu, stop);
+    if (stop) rpos[nr + __popc(bal & lanemask_lt())] = (uint16_t)j;
+    nr += __popc(bal);
+  }
+  __syncwarp();
+  // swaps happen for the prefix of m with lpos[m] < rpos[m] (monotone in m)
+  const int mmax = min(nl, nr);
+  int nsw = 0;
+  for (int base = 0; base < mmax; base += 32) {
+    int m = base + lane;
+    bool sw = (m < mmax) && (lpos[m] < rpos[m]);
+    nsw += __popc(__ballot_sync(0xffffffffu, sw));
+  }
+  // perform the swaps (disjoint positions)
+  for (int base = 0; base < nsw; base += 32) {
+    int m = base + lane;
+    float lv = 0.f, rv = 0.f;
+    uint16_t li = 0, ri = 0;
+    int L = 0, R = 0;
+    if (m < nsw) {
+      L = lpos[m];
+      R = rpos[m];
+      lv = a.v[L];
+      li = a.ix[L];
+      rv = a.v[R];
+      ri = a.ix[R];
+    }
+    __syncwarp();
+    if (m < nsw) {
+      a.v[L] = rv;
+      a.ix[L] = ri;
+      a.v[R] = lv;
+      a.ix[R] = li;
+    }
+    __syncwarp();
+  }
+  int cut = 0x7fffffff;
+  if (nsw < nl) cut = lpos[nsw];
+  if (nsw >= 1) cut = min(cut, (int)rpos[nsw - 1]);
+  __syncwarp();
+  return cut;
+}
+
+// Full torch-CPU topk replay on one row held in shared memory.  On return positions
+// [0,k) hold the result in torch's order.
+MSV_DEVICE void warp_topk_torch_cpu(Arr a, int n, int k, uint16_t* lpos, uint16_t* rpos) {
+  const int lane = threadIdx.x & 31;
+  if (k * 64 <= n) {  // std::partial_sort
+    if (lane == 0) {
+      heap_select(a, 0, k, n);
+      sort_heap(a, 0, k);
+    }
+    __syncwarp();
+    return;
+  }
+  // std::nth_element(first, first + k - 1, last) == __introselect(depth = 2*floor(log2 n))
+  int f = 0, l = n, nth = k - 1;
+  int depth = 2 * (31 - __clz(n));
+  bool done = false;
+  while (l - f > 3) {
+    if (depth == 0) {
+      if (lane == 0) {
+        heap_select(a, f, nth + 1, l);
+        a.swap(f, nth);
+      }
+      done = true;
+      break;
+    }
+    depth--;
+    const int mid = f + (l - f) / 2;
+    if (lane == 0) move_median_to_first(a, f, f + 1, mid, l - 1);
+    __syncwarp();
+    const float p = a.v[f];
+    const int cut = warp_partition(a, f + 1, l, p, lpos, rpos);
+    if (cut <= nth) f = cut;
+    else l = cut;
+  }
+  if (lane == 0) {
+    if (!done) insertion_sort(a, f, l);
+    // std::sort(first, first + k - 1): k - 1 <= 16 elements, i.e. one insertion sort
+    insertion_sort(a, 0, k - 1);
+  }
+  __syncwarp();
+}
+
+constexpr int kRouteWarps = 4;
+
+// One warp per token.  Shared memory per warp: n floats + 3n uint16.
+__global__ void __launch_bounds__(kRouteWarps * 32) k_route_topk(const float* __restrict__ logits, int64_t ld,
+                                                                  int T, int E, int k, int softmax, int renorm,
+                                                                  void* __restrict__ out_w, int w_dtype,
+                                                                  void* __restrict__ out_ids, int ids_dtype,
+                                                                  float* __restrict__ out_vals) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * kRouteWarps + warp;
+  if (t >= T) return;  // whole warp exits together
+  const int estride = (E + 7) & ~7;
+  float* v = reinterpret_cast<float*>(sm) + warp * estride;
+  uint16_t* ix = reinterpret_cast<uint16_t*>(reinterpret_cast<float*>(sm) + kRouteWarps * estride) + warp * 3 * estride;
+  uint16_t* lpos = ix + estride;
+  uint16_t* rpos = ix + 2 * estride;
+  const float* row = logits + (int64_t)t * ld;
+  float mx = -INFINITY;
+  bool any_nan = false;
+  for (int i = lane; i < E; i += 32) {
+    float x = row[i];
+    v[i] = x;
+    ix[i] = (uint16_t)i;
+    mx = fmaxf(mx, x);
+    any_nan |= (x != x);
+  }
+  mx = warp_max(mx);
+  any_nan = __any_sync(0xffffffffu, any_nan);
+  // torch's softmax turns a whole row into NaN when it holds a NaN or +inf logit; select on
+  // that all-NaN row then, exactly as torch.topk sees it.
+  const bool all_nan = softmax && (any_nan || mx == INFINITY);
+  float sum = 0.f;
+  if (softmax && !all_nan) {
+    for (int i = lane; i < E; i += 32) sum += expf(v[i] - mx);
+    sum = warp_sum(sum);
+  }
+  if (all_nan)
+    for (int i = lane; i < E; i += 32) v[i] = __int_as_float(0x7fffffff);
+  __syncwarp();
+  Arr a{v, ix};
+  warp_topk_torch_cpu(a, E, k, lpos, rpos);
+  // weights: score_j = exp(x_j - max) * (1/sum); optional renormalisation over the k
+  float s = 0.f;
+  uint16_t id = 0;
+  if (lane < k) {
+    id = ix[lane];
+    float x = v[lane];
+    s = softmax ? (all_nan ? x : expf(x - mx) * (1.0f / sum)) : x;
+  }
+  if (renorm) {
+    float tot = 0.f;
+    for (int j = 0; j < k; ++j) tot += __shfl_sync(0xffffffffu, s, j);  // slot order
+    s = __fdiv_rn(s, tot);
+  }
+  if (lane < k) {
+    const int64_t o = (int64_t)t * k + lane;
+    if (out_w) {
+      if (w_dtype == MSV_BF16) reinterpret_cast<__nv_bfloat16*>(out_w)[o] = __float2bfloat16_rn(s);
+      else reinterpret_cast<float*>(out_w)[o] = s;
+    }
+    if (out_vals) out_vals[o] = v[lane];
+    if (ids_dtype == MSV_I64) reinterpret_cast<int64_t*>(out_ids)[o] = id;
+    else reinterpret_cast<int32_t*>(out_ids)[o] = id;
+  }
+}
+
+size_t route_smem_bytes(int E) {
+  const int estride = (E + 7) & ~7;
+  return (size_t)kRouteWarps * estride * (4 + 3 * 2);
+}
+
+// ── dispatch bookkeeping ────────────────────────────────────────────────────────────────
+
+struct PermuteArgs {
+  const void* ids;
+  int ids_i64;
+  int T, k, num_experts, placement, tp, rank, alignment;
+  int e_local;
+  int64_t* sort_order;
+  int64_t* inverse_order;
+  int32_t* sorted_expert_ids;
+  int32_t* expert_counts;
+  int32_t* num_local;
+  int32_t* row_token;  // [T*k] token of each sorted row (internal)
+  int32_t* slot_row;   // [T*k] sorted row of each slot, -1 when not local (internal)
+  // grouped-GEMM tile lists (internal; nullptr to skip)
+  int4* tiles1;
+  int* ntiles1;
+  int bn1, nb1;
+  int4* tiles2;
+  int* ntiles2;
+  int bn2, nb2;
+  int shared_rows;    // > 0: append the shared-expert group (rows [row_base_shared, +shared_rows))
+  int row_base_shared;
+};
+
+constexpr int kPermThreads = 1024;
+constexpr int kPermWarps = kPermThreads / 32;
+
+MSV_DEVICE int load_id(const PermuteArgs& p, int f) {
+  return p.ids_i64 ? (int)reinterpret_cast<const int64_t*>(p.ids)[f] : reinterpret_cast<const int32_t*>(p.ids)[f];
+}
+
+// Tile list of one grouped GEMM: per local expert with c rows, ceil(c/bn) row chunks of
+// near-equal size (multiples of 16) times nb weight n-blocks, ordered expert, n-block, chunk
+// (chunks sharing a weight tile are adjacent).  The shared-expert group goes first.
+MSV_DEVICE void build_tiles(const PermuteArgs& p, const int* counts, const int* offsets, int* scratch, int4* tiles,
+                            int* ntiles, int bn, int nb) {
+  const int tid = threadIdx.x;
+  const int nsh_chunks = p.shared_rows > 0 ? (p.shared_rows + bn - 1) / bn : 0;
+  const int nsh = nsh_chunks * nb;
+  // per-expert tile counts, exclusive scan (sequential per 1024-chunk is enough: e_local <= 1024)
+  for (int e = tid; e < p.e_local; e += kPermThreads) {
+    int c = counts[e];
+    scratch[e] = c > 0 ? ((c + bn - 1) / bn) * nb : 0;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int run = nsh;
+    for (int e = 0; e < p.e_local; ++e) {
+      int n = scratch[e];
+      scratch[e] = run;
+      run += n;
+    }
+    *ntiles = run;
+  }
+  __syncthreads();
+  // shared-expert tiles
+  for (int i = tid; i < nsh; i += kPermThreads) {
+    int nbi = i / nsh_chunks, ch = i % nsh_chunks;
+    int cs = ((p.shared_rows + nsh_chunks - 1) / nsh_chunks + 15) & ~15;
+    int r0 = ch * cs;
+    int nr = min(cs, p.shared_rows - r0);
+    tiles[i] = make_int4(p.row_base_shared + r0, nr, (1 << 24) | 0, nbi);
+  }
+  for (int e = tid; e < p.e_local; e += kPermThreads) {
+    int c = counts[e];
+    if (c == 0) continue;
+    int nch = (c + bn - 1) / bn;
+    int cs = ((c + nch - 1) / nch + 15) & ~15;
+    int base = scratch[e];
+    for (int nbi = 0; nbi < nb; ++nbi)
+      for (int ch = 0; ch < nch; ++ch) {
+        int r0 = ch * cs;
+        int nr = min(cs, c - r0);
+        if (nr <= 0) nr = 0;
+        tiles[base + nbi * nch + ch] = make_int4(offsets[e] + r0, nr, e, nbi);
+      }
+  }
+  __syncthreads();
+}
+
+// One CTA.  Warp w owns the contiguous slot chunk [w*C, (w+1)*C): pass 1 counts local slots
+// per (warp, expert); the scan turns the counts into each (warp, expert) base row; pass 2
+// walks the chunk in order and ranks equal experts inside each 32-slot batch with
+// __match_any_sync, which keeps the sort stable.
+__global__ void __launch_bounds__(kPermThreads) k_permute(PermuteArgs p) {
+  extern __shared__ __align__(16) int hist[];  // [kPermWarps][e_local], then scratch
+  __shared__ int s_nloc[kPermWarps];
+  __shared__ int s_total;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int E = p.e_local;
+  int* counts = hist + kPermWarps * E;   // [E]
+  int* offsets = counts + E;             // [E+1]
+  int* scratch = offsets + E + 1;        // [E]
+  const int P = p.T * p.k;
+  const int C = (P + kPermWarps - 1) / kPermWarps;
+  const int c0 = min(P, warp * C), c1 = min(P, c0 + C);
+  for (int i = threadIdx.x; i < kPermWarps * E; i += kPermThreads) hist[i] = 0;
+  __syncthreads();
+  int nloc = 0;
+  for (int f = c0 + lane; f < c1; f += 32) {
+    int e = load_id(p, f);
+    bool local = p.placement == 0 || (e % p.tp) == p.rank;
+    int le = p.placement == 0 ? e : e / p.tp;
+    if (local && le >= 0 && le < E) {
+      atomicAdd(&hist[warp * E + le], 1);
+      nloc++;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) nloc += __shfl_xor_sync(0xffffffffu, nloc, o);
+  if (lane == 0) s_nloc[warp] = nloc;
+  __syncthreads();
+  // per-expert totals
+  for (int e = threadIdx.x; e < E; e += kPermThreads) {
+    int c = 0;
+    for (int w = 0; w < kPermWarps; ++w) c += hist[w * E + e];
+    counts[e] = c;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int e = 0; e < E; ++e) {
+      offsets[e] = run;
+      run += counts[e];
+    }
+    offsets[E] = run;
+    s_total = run;
+    *p.num_local = run;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += kPermThreads) {
+    int run = offsets[e];
+    for (int w = 0; w < kPermWarps; ++w) {
+      int c = hist[w * E + e];
+      hist[w * E + e] = run;
+      run += c;
+    }
+    if (p.expert_counts) p.expert_counts[e] = counts[e];
+  }
+  int lpbase = 0;
+  for (int w = 0; w < warp; ++w) lpbase += s_nloc[w];
+  __syncthreads();
+  for (int b0 = c0; b0 < c1; b0 += 32) {
+    const int f = b0 + lane;
+    const bool valid = f < c1;
+    int e = valid ? load_id(p, f) : -1;
+    int le = p.placement == 0 ? e : (e >= 0 ? e / p.tp : -1);
+    bool local = valid && (p.placement == 0 || (e % p.tp) == p.rank) && le >= 0 && le < E;
+    uint32_t bal = __ballot_sync(0xffffffffu, local);
+    int lp = lpbase + __popc(bal & lanemask_lt());
+    lpbase += __popc(bal);
+    uint32_t key = local ? (uint32_t)le : 0xffffffffu;
+    uint32_t peers = __match_any_sync(0xffffffffu, key);
+    int r = 0;
+    if (local) r = hist[warp * E + le] + __popc(peers & lanemask_lt());
+    __syncwarp();
+    if (local && (__ffs(peers) - 1) == lane) hist[warp * E + le] += __popc(peers);
+    __syncwarp();
+    if (valid) {
+      if (p.slot_row) p.slot_row[f] = local ? r : -1;
+      if (local) {
+        if (p.row_token) p.row_token[r] = f / p.k;
+        if (p.sort_order) p.sort_order[r] = lp;
+        if (p.inverse_order) p.inverse_order[lp] = r;
+        if (p.sorted_expert_ids) p.sorted_expert_ids[r] = le;
+      }
+    }
+  }
+  __syncthreads();
+  if (p.sorted_expert_ids && p.alignment > 0) {
+    const int nl = s_total;
+    const int padded = ((nl + p.alignment - 1) / p.alignment) * p.alignment;
+    for (int r = nl + threadIdx.x; r < padded; r += kPermThreads) p.sorted_expert_ids[r] = -1;
+  }
+  if (p.tiles1) build_tiles(p, counts, offsets, scratch, p.tiles1, p.ntiles1, p.bn1, p.nb1);
+  if (p.tiles2) build_tiles(p, counts, offsets, scratch, p.tiles2, p.ntiles2, p.bn2, p.nb2);
+}
+
+size_t permute_smem_bytes(int e_local) { return (size_t)(kPermWarps * e_local + 3 * e_local + 1) * sizeof(int); }
+
+// Groups from an arbitrary per-row expert array (the ragged-GEMM shim): every maximal run
+// of equal non-negative ids is one group, chunked by bn, times nb n-blocks.  One CTA.
+__global__ void __launch_bounds__(1024) k_tiles_from_runs(const int32_t* __restrict__ m_indices, int M, int bn,
+                                                          int nb, int4* __restrict__ tiles, int* __restrict__ ntiles,
+                                                          int cap) {
+  __shared__ int s_base;
+  __shared__ int s_warp[32];
+  if (threadIdx.x == 0) s_base = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int b0 = 0; b0 < M; b0 += 1024) {
+    const int m = b0 + threadIdx.x;
+    int e = -1, len = 0;
+    if (m < M) {
+      e = m_indices[m];
+      bool start = e >= 0 && (m == 0 || m_indices[m - 1] != e);
+      if (start) {
+        int j = m + 1;
+        while (j < M && m_indices[j] == e) ++j;
+        len = j - m;
+      }
+    }
+    int nt = len > 0 ? ((len + bn - 1) / bn) * nb : 0;
+    // block exclusive scan of nt
+    int incl = nt;
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) s_warp[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      int v = s_warp[lane];
+      int vi = v;
+      for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, vi, o);
+        if (lane >= o) vi += y;
+      }
+      s_warp[lane] = vi - v;
+    }
+    __syncthreads();
+    int pos = s_base + s_warp[warp] + incl - nt;
+    if (len > 0) {
+      int nch = (len + bn - 1) / bn;
+      int cs = ((len + nch - 1) / nch + 15) & ~15;
+      for (int nbi = 0; nbi < nb; ++nbi)
+        for (int ch = 0; ch < nch; ++ch) {
+          int r0 = ch * cs;
+          int nr = min(cs, len - r0);
+          int ti = pos + nbi * nch + ch;
+          if (ti < cap) tiles[ti] = make_int4(m + r0, max(nr, 0), e, nbi);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 1023) s_base = pos + nt;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *ntiles = min(s_base, cap);
+}
+
+}  // namespace msv
+
+namespace msv {
+// Tile list of a dense GEMM: one group of M rows chunked by bn, times nb n-blocks.
+__global__ void k_tiles_dense(int M, int bn, int nb, int4* __restrict__ tiles, int* __restrict__ ntiles) {
+  const int nch = (M + bn - 1) / bn;
+  const int n = nch * nb;
+  const int cs = ((M + nch - 1) / nch + 15) & ~15;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int nbi = i / nch, ch = i % nch;
+    const int r0 = ch * cs;
+    tiles[i] = make_int4(r0, max(0, min(cs, M - r0)), 0, nbi);
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) *ntiles = n;
+}
+}  // namespace msv

@@ -1,0 +1,75 @@
+"""MoE half of the reference's active layer (``muserve/model/qwen35_layer_v2.py``) on sm_100a.
+
+``moe_forward(hidden, weights)`` keeps the reference's signature and weights-dict contract
+(``:561``, ``loader.py:212-264``).  The router GEMM stays ``F.linear`` in bf16 (``:568``, a
+plain cuBLAS GEMM); everything after it runs in the library's six kernels (router top-k,
+dispatch, gather+quantise, gate_up GEMM with SwiGLU+requant epilogue, down GEMM, combine +
+shared expert).  With tensor parallelism the per-rank partial ``[T,H]`` is all-reduced once
+(the V1 / BASELINE placement, ``qwen35_layer.py:565-571``) instead of V2's ``[T*k,H]``
+buffer (``:652-657``); results differ from V2 only by bf16 rounding of partial sums.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from .. import config, moe
+from ..distributed import all_reduce, get_tp_rank, get_tp_size
+
+
+def _fast_fp8_quantize(x: torch.Tensor, block_size: int = 128):
+    """Per-token per-128-channel e4m3 quantisation (``:71-86``): ``(x_fp8 [M,K], x_scale [M,K/128])``."""
+    assert block_size == 128, "only 128-channel blocks"
+    orig = x.shape
+    x2 = x.reshape(-1, orig[-1])
+    assert x2.shape[1] % block_size == 0, f"K={x2.shape[1]} not divisible by block_size={block_size}"
+    q, s = moe.fp8_quant_128(x2.contiguous())
+    return q, s
+
+
+def fp8_linear(x: torch.Tensor, w_fp8: torch.Tensor, w_scale: torch.Tensor) -> torch.Tensor:
+    """``x [..., K] @ w [N, K]^T`` with dynamic per-128 activation quantisation (``:89-107``)."""
+    orig = x.shape
+    xq, xs = _fast_fp8_quantize(x.reshape(-1, orig[-1]))
+    out = moe.gemm_nt(xq, xs, w_fp8, w_scale)
+    return out.reshape(*orig[:-1], w_fp8.shape[0])
+
+
+def bf16_linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """``F.linear`` in bf16 (``:110-112``)."""
+    return F.linear(x, w)
+
+
+def linear_maybe_fp8(x: torch.Tensor, weights: dict, prefix: str) -> torch.Tensor:
+    w = weights[f"{prefix}.weight"]
+    s = weights.get(f"{prefix}.weight_scale_inv")
+    return fp8_linear(x, w, s) if s is not None else bf16_linear(x, w)
+
+
+def _layout(weights: dict, num_experts: int, tp: int) -> str:
+    lay = weights.get("moe.layout")
+    if lay is not None:
+        return lay
+    if tp == 1:
+        return "inter"
+    w = weights.get("moe.experts.gate_proj.weight", weights.get("moe.experts.gate_up_proj.weight"))
+    return "expert" if w.shape[0] * tp == num_experts else "inter"
+
+
+def moe_forward(hidden: torch.Tensor, weights: dict, *, top_k: int | None = None,
+                return_routing: bool = False) -> torch.Tensor:
+    """MoE forward. hidden: [total, HIDDEN] bf16 -> output: [total, HIDDEN] bf16 (``:561-675``)."""
+    k = top_k if top_k is not None else config.NUM_EXPERTS_PER_TOK
+    gate_w = weights["moe.gate.weight"]
+    num_experts = gate_w.shape[0]
+    tp, rank = get_tp_size(), get_tp_rank()
+    logits = bf16_linear(hidden, gate_w).float()                               # :568
+    lay = _layout(weights, num_experts, tp)
+    placement = 1 if (tp > 1 and lay == "expert") else 0
+    res = moe.moe_layer(hidden.contiguous(), weights, top_k=k, num_experts=num_experts, router_logits=logits,
+                        placement=placement, tp=tp, rank=rank,
+                        add_shared=(placement == 0 or rank == 0), return_routing=return_routing)
+    out = res[0] if return_routing else res
+    if tp > 1:
+        all_reduce(out)
+    return res if return_routing else out

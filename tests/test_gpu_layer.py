@@ -1,0 +1,166 @@
+"""Whole MoE layer on the GPU vs the reference (golden fixtures) and the CPU oracle, from the
+BASELINE CPU-check config to full-shape decode (64 tokens) and prefill (8192 tokens)."""
+import pytest
+import torch
+
+from conftest import assert_close_bf16, load_golden, max_abs_rel
+from muserve_b200 import _lib, moe, synthetic
+from muserve_b200.kernels.batched_moe import batched_moe_forward
+from muserve_b200.kernels.moe_dispatch import moe_experts_fp8
+from muserve_b200.model import qwen35_layer_v2 as v2
+from oracle import moe_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+
+def to_dev(w, dev):
+    return {k: (v.to(dev) if torch.is_tensor(v) else v) for k, v in w.items()}
+
+
+@pytest.fixture(scope="module")
+def c0(cuda):
+    g = load_golden("c0")
+    c = g["cfg"]
+    w = orc.make_layer_weights(c["hidden"], c["experts"], c["inter"], c["shared"], seed=c["wseed"])
+    x = orc.make_hidden(c["tokens"], c["hidden"], c["xseed"])
+    return g, c, w, x, to_dev(w, cuda), x.to(cuda)
+
+
+def test_layer_c0_on_reference_logits(c0):
+    """Identical router logits -> identical routing; the output matches the reference's own
+    moe_forward within the bf16 bar."""
+    g, c, w, x, wd, xd = c0
+    out, tw, tid = moe.moe_layer(xd, wd, top_k=c["k"], num_experts=c["experts"],
+                                 router_logits=g["logits"].to(xd.device), return_routing=True)
+    assert torch.equal(tid.cpu().long(), g["topk_ids"])
+    assert_close_bf16(out, g["output"])
+    moe.check_device_error()
+
+
+def test_moe_forward_c0_end_to_end(c0):
+    """Through the reference-shaped moe_forward (router GEMM on cuBLAS): routing compared to
+    the reference separately, output compared on tokens routed identically."""
+    g, c, w, x, wd, xd = c0
+    out, tw, tid = v2.moe_forward(xd, wd, top_k=c["k"], return_routing=True)
+    same = (tid.cpu().long() == g["topk_ids"]).all(-1)
+    assert same.float().mean() >= 0.9, f"routing differs on {int((~same).sum())} of {len(same)} tokens"
+    assert_close_bf16(out.cpu()[same], g["output"][same])
+
+
+def test_layer_small_golden_intermediates(cuda):
+    g = load_golden("small")
+    c = g["cfg"]
+    w = orc.make_layer_weights(c["hidden"], c["experts"], c["inter"], c["shared"], seed=c["wseed"])
+    wd = to_dev(w, cuda)
+    # gate_up GEMM through the ragged shim on the reference's own quantised rows
+    gu_w = torch.cat([w["moe.experts.gate_proj.weight"], w["moe.experts.up_proj.weight"]], 1)
+    gu_s = torch.cat([w["moe.experts.gate_proj.weight_scale_inv"], w["moe.experts.up_proj.weight_scale_inv"]], 1)
+    out = torch.zeros_like(g["gate_up"]).to(cuda)
+    moe.ragged_gemm(g["x_fp8"].to(cuda), g["x_scale"].to(cuda), gu_w.to(cuda), gu_s.to(cuda),
+                    g["sorted_expert_ids"].to(cuda), out)
+    nl = g["num_local"]
+    assert_close_bf16(out[:nl], g["gate_up"][:nl])
+    # requantisation of the reference's activation is bit-exact
+    act = torch.nn.functional.silu(g["gate_up"][:, :c["inter"]]) * g["gate_up"][:, c["inter"]:]
+    act[nl:] = 0
+    q, s = moe.fp8_quant_128(act.to(cuda))
+    assert torch.equal(q.cpu().view(torch.uint8), g["act_fp8"].view(torch.uint8))
+    assert torch.equal(s.cpu(), g["act_scale"])
+    x = orc.make_hidden(c["tokens"], c["hidden"], c["xseed"]).to(cuda)
+    o = moe.moe_layer(x, wd, top_k=c["k"], num_experts=c["experts"], router_logits=g["logits"].to(cuda))
+    assert_close_bf16(o, g["output"])
+
+
+def test_kernel_layer_apis(c0):
+    """moe_experts_fp8 and batched_moe_forward keep their reference accumulation order."""
+    g, c, w, x, wd, xd = c0
+    ids = g["topk_ids"].int()
+    tw32 = torch.softmax(g["logits"], -1).gather(1, g["topk_ids"])
+    tw32 = tw32 / tw32.sum(-1, keepdim=True)
+    gu_w = torch.cat([w["moe.experts.gate_proj.weight"], w["moe.experts.up_proj.weight"]], 1)
+    gu_s = torch.cat([w["moe.experts.gate_proj.weight_scale_inv"], w["moe.experts.up_proj.weight_scale_inv"]], 1)
+    out = moe_experts_fp8(xd, ids.to(xd.device), tw32.to(xd.device), gu_w.to(xd.device), gu_s.to(xd.device),
+                          wd["moe.experts.down_proj.weight"], wd["moe.experts.down_proj.weight_scale_inv"])
+    routed_only = {k: v for k, v in w.items() if not k.startswith("moe.shared")}
+    ref = orc.moe_forward_tokens(x, routed_only, tw32, g["topk_ids"], combine="dispatch")
+    assert_close_bf16(out, ref)
+    out_b = batched_moe_forward(xd, dict(wd), top_k=c["k"])
+    lg = torch.nn.functional.linear(xd, wd["moe.gate.weight"]).float()
+    tw_b, tid_b = orc.route(lg.cpu(), c["k"])
+    ref_b = orc.moe_forward_tokens(x, w, tw_b, tid_b, combine="batched")
+    assert_close_bf16(out_b, ref_b)
+
+
+# ── full shapes (BASELINE configs 1 and 2) ─────────────────────────────────────────────────
+
+@pytest.fixture(scope="module")
+def full_layer(cuda):
+    w = synthetic.make_layer_weights(4096, 512, 1024, 1024, seed=1, device=cuda)
+    yield w
+    del w
+    torch.cuda.empty_cache()
+
+
+def expert_fetch(w):
+    def fn(e):
+        gu = torch.cat([w["moe.experts.gate_proj.weight"][e], w["moe.experts.up_proj.weight"][e]], 0).cpu()
+        gs = torch.cat([w["moe.experts.gate_proj.weight_scale_inv"][e], w["moe.experts.up_proj.weight_scale_inv"][e]],
+                       0).cpu()
+        return gu, gs, w["moe.experts.down_proj.weight"][e].cpu(), w["moe.experts.down_proj.weight_scale_inv"][e].cpu()
+    return fn
+
+
+def shared_cpu(w):
+    return {k: v.cpu() for k, v in w.items() if k.startswith("moe.shared")}
+
+
+def check_sample(x, w, out, tw, tid, tokens):
+    xs = x[tokens].cpu()
+    ref = orc.moe_forward_tokens(xs, shared_cpu(w), tw[tokens].cpu(), tid[tokens].cpu().long(),
+                                 expert_fn=expert_fetch(w))
+    assert_close_bf16(out[tokens].cpu(), ref)
+
+
+def test_full_decode_c1(cuda, full_layer):
+    """64 tokens, uniform random router logits, 512 experts top-10 + shared expert."""
+    w = full_layer
+    x = synthetic.make_hidden(64, 4096, seed=2, device=cuda)
+    logits = synthetic.uniform_logits(64, 512, seed=3, device=cuda)
+    out, tw, tid = moe.moe_layer(x, w, top_k=10, num_experts=512, router_logits=logits, return_routing=True)
+    rw, rid = orc.route(logits.cpu(), 10)
+    assert torch.equal(tid.cpu().long(), rid)
+    assert (tw.cpu().view(torch.int16).int() - rw.view(torch.int16).int()).abs().max() <= 1
+    check_sample(x, w, out, tw, tid, torch.tensor([0, 1, 17, 40, 63]))
+    assert torch.isfinite(out.float()).all()
+    moe.check_device_error()
+
+
+def test_full_prefill_c2(cuda, full_layer):
+    """8192 tokens, router gate N(0, 0.02): ~160 tokens per expert, multi-chunk tiles."""
+    w = full_layer
+    x = synthetic.make_hidden(8192, 4096, seed=4, device=cuda)
+    out, tw, tid = v2.moe_forward(x, w, top_k=10, return_routing=True)
+    counts = torch.bincount(tid.flatten().long(), minlength=512)
+    assert counts.sum() == 8192 * 10 and counts.max() > 128  # exercises the chunked tiles
+    check_sample(x, w, out, tw, tid, torch.tensor([0, 5, 1000, 4097, 8191]))
+    moe.check_device_error()
+
+
+def test_full_zipf_skew(cuda, full_layer):
+    """Skewed popularity (Zipf 1.2 prior on the logits): some experts get
+    hundreds of rows in a 128-token batch and are split in chunks."""
+    w = full_layer
+    x = synthetic.make_hidden(128, 4096, seed=6, device=cuda)
+    lg = torch.nn.functional.linear(x, w["moe.gate.weight"]).float() + synthetic.zipf_bias(512, device=cuda)
+    out, tw, tid = moe.moe_layer(x, w, top_k=10, num_experts=512, router_logits=lg.contiguous(), return_routing=True)
+    counts = torch.bincount(tid.flatten().long(), minlength=512)
+    assert counts.max() > 32
+    check_sample(x, w, out, tw, tid, torch.tensor([0, 64, 127]))
+
+
+def test_layer_deterministic(cuda, full_layer):
+    x = synthetic.make_hidden(64, 4096, seed=2, device=cuda)
+    logits = synthetic.uniform_logits(64, 512, seed=3, device=cuda)
+    a = moe.moe_layer(x, full_layer, top_k=10, num_experts=512, router_logits=logits)
+    b = moe.moe_layer(x, full_layer, top_k=10, num_experts=512, router_logits=logits)
+    assert torch.equal(a, b)

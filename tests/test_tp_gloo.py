@@ -1,0 +1,64 @@
+"""Multi-rank host path on CPU: world_size-2 gloo process groups through
+muserve_b200.distributed (the NCCL path's plumbing), with the reference's known-answer
+all-reduce test (muserve/scripts/test_allreduce.py:31-43) and the intermediate-sharded layer."""
+import os
+import socket
+import tempfile
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, outdir):
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    from muserve_b200 import distributed as D
+    from muserve_b200 import loader
+    from oracle import moe_oracle as orc
+    D.init_distributed(backend="gloo", timeout_s=60)
+    assert D.get_tp_rank() == rank and D.get_tp_size() == world
+    # known answer: every rank fills rank+1, the sum is n(n+1)/2, 100 rounds
+    for _ in range(100):
+        x = torch.full((4096,), float(rank + 1), dtype=torch.bfloat16)
+        D.all_reduce(x)
+        assert (x == world * (world + 1) // 2).all()
+    # intermediate-sharded layer: per-rank partial, one all-reduce
+    w = orc.make_layer_weights(256, 16, 256, 256, seed=3)
+    hid = orc.make_hidden(16, 256, 4)
+    part = orc.moe_forward(hid, loader.shard_moe_weights(w, world, rank, "inter"), 16, 4).float()
+    D.all_reduce(part)
+    torch.save(part.to(torch.bfloat16), os.path.join(outdir, f"out{rank}.pt"))
+    D.barrier()
+    D.destroy_distributed()
+
+
+@pytest.mark.timeout(300)
+def test_gloo_two_ranks():
+    outdir = tempfile.mkdtemp()
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, outdir)) for r in range(2)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(240)
+        assert p.exitcode == 0
+    from conftest import assert_close_bf16
+    from oracle import moe_oracle as orc
+    o0 = torch.load(os.path.join(outdir, "out0.pt"))
+    o1 = torch.load(os.path.join(outdir, "out1.pt"))
+    assert torch.equal(o0, o1)
+    w = orc.make_layer_weights(256, 16, 256, 256, seed=3)
+    ref = orc.moe_forward(orc.make_hidden(16, 256, 4), w, 16, 4)
+    assert_close_bf16(o0, ref)
