@@ -58,13 +58,20 @@ class Clocks:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t0 = time.time()
+            while not self.rows and time.time() - t0 < 5:  # sampler running before timing starts
+                time.sleep(0.02)
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
+
+    def mark(self, on: bool):
+        self.active = on
+        self.rows.append(["mark", "on" if on else "off"])
 
     def _read(self):
         for line in self.proc.stdout:
@@ -79,6 +86,16 @@ class Clocks:
                 self.proc.kill()
 
     def summary(self):
+        # samples between the marks (the timed region), else all samples
+        rows, inside, sel = self.rows, False, []
+        for r in rows:
+            if r[0] == "mark":
+                inside = r[1] == "on"
+                continue
+            if inside:
+                sel.append(r)
+        rows = sel or [r for r in rows if r[0] != "mark"]
+        self.rows = rows
         if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
@@ -155,7 +172,8 @@ def run_ours(args, world, rank, local):
     tokens = args.tokens or (8192 if prefill else (64 if world == 1 else 256))
     tp = world
     # weights: the full layer from one seed on every rank, then this rank's intermediate shard
-    w = synthetic.make_layer_weights(H, E, INTER, SHARED, seed=1, device=dev)
+    n_exp = args.experts or E
+    w = synthetic.make_layer_weights(H, n_exp, INTER, SHARED, seed=1, device=dev)
     if tp > 1:
         w = shard_moe_weights(w, tp, rank, "inter")
         torch.cuda.empty_cache()
@@ -165,9 +183,9 @@ def run_ours(args, world, rank, local):
     if prefill:
         logits = torch.nn.functional.linear(x, w["moe.gate.weight"]).float().contiguous()
     else:
-        logits = synthetic.uniform_logits(tokens, E, seed=3, device=dev)
+        logits = synthetic.uniform_logits(tokens, n_exp, seed=3, device=dev)
     ws_struct, info = moe.weights_struct(w)
-    shape = _lib.MoeShape(tokens=tokens, hidden=H, num_experts=E, top_k=K_TOP, inter=inter, shared_inter=shared,
+    shape = _lib.MoeShape(tokens=tokens, hidden=H, num_experts=n_exp, top_k=K_TOP, inter=inter, shared_inter=shared,
                           placement=0, tp=1, rank=0, add_shared=1, combine_mode=_lib.COMBINE_V2,
                           weights_dtype=_lib.MSV_BF16)
     nbytes = lib.msv_moe_forward_workspace_size(ctypes.byref(shape))
@@ -207,7 +225,7 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize()
     _lib.check(lib.msv_check_device_error(sp), "warmup")
     # routing statistics of the measured step (identical every step)
-    counts = torch.bincount(tid.flatten().long(), minlength=E)
+    counts = torch.bincount(tid.flatten().long(), minlength=n_exp)
     n_touched = int((counts > 0).sum().item())
     rows = tokens * K_TOP + tokens
     barrier()
@@ -215,11 +233,16 @@ def run_ours(args, world, rank, local):
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
+        for _ in range(args.warmup):  # keep the GPU busy while the sampler settles
+            step()
+        torch.cuda.synchronize()
+        clk.mark(True)
         t0.record(stream)
         for i in range(args.steps):
             step(i)
         t1.record(stream)
         torch.cuda.synchronize()
+        clk.mark(False)
     barrier()
     ms_total = max_over_ranks(t0.elapsed_time(t1))
     _lib.check(lib.msv_check_device_error(sp), "timed region")
@@ -235,6 +258,8 @@ def run_ours(args, world, rank, local):
     layer_gbs = layer_bytes(n_touched, inter, shared, tokens) / (ms_step / 1e3) / 1e9
     flops = 6 * H * inter * tokens * K_TOP + 6 * H * shared * tokens
     workload = ("prefill_c2" if prefill else "decode_c1") if tp == 1 else f"tp{tp}_decode_c3"
+    if n_exp != E:
+        workload += f"_e{n_exp}"
 
     # e2e: through the reference-facing API from pinned host buffers, result read back each step
     e2e = None
@@ -249,7 +274,7 @@ def run_ours(args, world, rank, local):
         def e2e_step():
             dx.copy_(hx, non_blocking=True)
             dl.copy_(hl, non_blocking=True)
-            o = M.moe_layer(dx, w, top_k=K_TOP, num_experts=E, router_logits=dl)
+            o = M.moe_layer(dx, w, top_k=K_TOP, num_experts=n_exp, router_logits=dl)
             if tp > 1:
                 dist.all_reduce(o)
             ho.copy_(o, non_blocking=True)
@@ -278,7 +303,7 @@ def run_ours(args, world, rank, local):
         "scaling": "strong", "vs_baseline": None, "dtype": "e4m3 x e4m3 -> fp32 acc, bf16 io",
         "data": "synthetic (seeded N(0,1) hidden, N(0,0.02) block-quantised weights, " +
                 ("router GEMM logits)" if prefill else "uniform random router logits)"),
-        "config": {"workload": workload, "tokens": tokens, "hidden": H, "experts": E, "top_k": K_TOP,
+        "config": {"workload": workload, "tokens": tokens, "hidden": H, "experts": n_exp, "top_k": K_TOP,
                    "inter_per_rank": inter, "shared_inter_per_rank": shared, "tp": tp,
                    "parallelism": f"tp{tp}" if tp > 1 else "single",
                    "l2": f"no flush: each step streams {layer_bytes(n_touched, inter, shared, tokens) / 1e9:.2f} GB"
@@ -386,6 +411,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill"])
     ap.add_argument("--tokens", type=int, default=0)
+    ap.add_argument("--experts", type=int, default=0, help="smaller expert count, for profiler captures only")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

@@ -139,9 +139,9 @@ int tensor_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t cols,
 // ── grouped GEMM variants ────────────────────────────────────────────────────────────────
 
 using G1Small = GemmCfg<32, 2, 1, 1>;   // gate+up -> SwiGLU -> e4m3, <= 32 rows per chunk
-using G1Large = GemmCfg<128, 2, 1, 4>;  // same, <= 128 rows per chunk
+using G1Large = GemmCfg<96, 2, 1, 3>;   // same, <= 96 rows per chunk (3 epilogue warpgroups)
 using G2Small = GemmCfg<32, 1, 0, 1>;   // plain -> bf16, <= 32 rows per chunk
-using G2Large = GemmCfg<256, 1, 0, 4>;  // plain -> bf16, <= 256 rows per chunk
+using G2Large = GemmCfg<192, 1, 0, 3>;  // plain -> bf16, <= 192 rows per chunk
 
 template <class C>
 int launch_gemm(const GemmArgs& a, cudaStream_t st, int num_sms) {

@@ -16,8 +16,10 @@
 namespace msv {
 
 // Every device-side wait gives up after this long and reports MSV_ERR_TIMEOUT through the
-// kernel's error word; nothing in these kernels can spin forever.
+// kernel's error word; nothing in these kernels can spin forever.  Hot-path waits count SM
+// cycles (clock64, cheap to read); 4e9 cycles is about 2 s at the B200's 1.97 GHz.
 constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;  // 2 s
+constexpr long long kWaitTimeoutCycles = 4000000000ll;
 
 // ── numerics ────────────────────────────────────────────────────────────────────────────
 
@@ -104,12 +106,12 @@ MSV_DEVICE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // *abort) when the wait runs out or another role of the CTA already aborted.
 MSV_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   if (mbar_try_wait(bar, parity)) return true;
-  unsigned long long t0 = globaltimer();
+  const long long t0 = clock64();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 63) == 0) {
       if (*abort) return false;
-      if (globaltimer() - t0 > kWaitTimeoutNs) {
+      if (clock64() - t0 > kWaitTimeoutCycles) {
         *abort = 1;
         return false;
       }
@@ -191,6 +193,26 @@ MSV_DEVICE void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
+// Warp-wide load of 32 consecutive fp32 columns of this warp's 32 TMEM lanes.
+MSV_DEVICE void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+MSV_DEVICE void tmem_ld16p(uint32_t taddr, float* v) {
+  float t[16];
+  tmem_ld16(taddr, *reinterpret_cast<float(*)[16]>(t));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = t[i];
+}
 MSV_DEVICE void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 MSV_DEVICE void named_bar_sync(int id, int nthreads) {
@@ -200,5 +222,11 @@ MSV_DEVICE void named_bar_sync(int id, int nthreads) {
 MSV_DEVICE void cp_async_4(void* dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
+// Arrive on `bar` once this thread's earlier cp.async copies have landed (the barrier's
+// expected count includes this arrival).
+MSV_DEVICE void cp_async_mbar_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+MSV_DEVICE void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 }  // namespace msv

@@ -61,21 +61,29 @@ struct GemmCfg {
                                    : COLS_USED <= 256 ? 256 : 512;
   static constexpr int CW = BN / NWG;
   static constexpr int THREADS = 128 + 128 * NWG;
-  static constexpr int SCL_BYTES = NBUF * NACC * BN * 4;
+  static constexpr int SCL_BYTES = 0;
   static constexpr int RED_BYTES = EPI == 1 ? NWG * 4 * CW * 4 : 0;
-  static constexpr int TAIL_BYTES = SCL_BYTES + RED_BYTES + 64 * 8 + 64;
+  static constexpr int SLOT_FLOATS = BN + 4;  // per K-block step: a_scale of the chunk's rows, then w_scale per acc
+  static constexpr int NSLOT_MAX = 20;
+  static constexpr int TAIL_BYTES = SCL_BYTES + RED_BYTES + 128 * 8 + 64 + NSLOT_MAX * SLOT_FLOATS * 4;
   static constexpr int SMEM_LIMIT = 232448 - 1024;  // 227 KB opt-in, minus alignment slack
   static constexpr int NSTAGE_RAW = (SMEM_LIMIT - TAIL_BYTES) / STAGE_BYTES;
   static constexpr int NSTAGE = NSTAGE_RAW > 12 ? 12 : NSTAGE_RAW;
   static constexpr int OFF_SCL = NSTAGE * STAGE_BYTES;
   static constexpr int OFF_RED = OFF_SCL + SCL_BYTES;
-  static constexpr int OFF_BAR = (OFF_RED + RED_BYTES + 7) & ~7;
-  static constexpr int NBARS = 2 * NSTAGE + 2 * NBUF + 1 + NWG;
+  // scale slots outlive their smem stage (the epilogue reads them after the MMA released the
+  // stage), so they form their own ring with ready/free barriers
+  static constexpr int NSLOT = NSTAGE + NBUF + 2 <= NSLOT_MAX ? NSTAGE + NBUF + 2 : NSLOT_MAX;
+  static constexpr int OFF_SLOT = OFF_RED + RED_BYTES;
+  static constexpr int OFF_BAR = (OFF_SLOT + NSLOT * SLOT_FLOATS * 4 + 7) & ~7;
+  static constexpr int NISSUE = 2;  // MMA-issuing warps (1, 2), taking alternate K blocks
+  static constexpr int NBARS = 2 * NSTAGE + 2 * NBUF + NISSUE + NWG + 2 * NSLOT;
   static constexpr int OFF_MISC = OFF_BAR + NBARS * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
-  static_assert(CW % 16 == 0, "column slice must be whole 16-column TMEM loads");
+  static_assert(CW % 32 == 0, "column slice must be whole 32-column TMEM loads");
   static_assert(NBUF >= 2, "need at least double-buffered TMEM partials");
   static_assert(NSTAGE >= 2, "pipeline too shallow");
+  static_assert(NSLOT > NSTAGE + NBUF, "scale ring must outlast the stage ring plus the TMEM ring");
   static_assert(SMEM_BYTES <= 232448, "shared memory over the sm_100 limit");
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
 };
@@ -94,26 +102,33 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* scl = reinterpret_cast<float*>(smem + C::OFF_SCL);
   float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
+  float* slots = reinterpret_cast<float*>(smem + C::OFF_SLOT);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* empty = full + NSTAGE;
   uint64_t* accf = empty + NSTAGE;
   uint64_t* acce = accf + NBUF;
-  uint64_t* drain = acce + NBUF;
-  uint64_t* epib = drain + 1;  // per epilogue warpgroup: 4 warps meet here (bounded)
+  uint64_t* drain = acce + NBUF;      // one per issuing warp
+  uint64_t* epib = drain + C::NISSUE;  // per epilogue warpgroup: 4 warps meet here (bounded)
+  uint64_t* sready = epib + C::NWG;    // scale slot landed (one cp.async arrival per producer lane)
+  uint64_t* sfree = sready + C::NSLOT; // scale slot consumed (one arrival per epilogue warp)
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < NSTAGE; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], 1);  // TMA expect_tx
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < NBUF; ++b) {
-      mbar_init(&accf[b], 2);           // MMA commit + scale staging
+      mbar_init(&accf[b], 1);           // MMA commit
       mbar_init(&acce[b], 4 * C::NWG);  // one arrive per epilogue warp
     }
-    mbar_init(drain, 1);
+    for (int j = 0; j < C::NSLOT; ++j) {
+      mbar_init(&sready[j], 32);
+      mbar_init(&sfree[j], 4 * C::NWG);
+    }
+    for (int i = 0; i < C::NISSUE; ++i) mbar_init(&drain[i], 1);
     for (int g = 0; g < C::NWG; ++g) mbar_init(&epib[g], 4);
     *s_abort = 0;
     fence_mbar_init();
@@ -131,35 +146,55 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
   const int nkb = args.num_kb;
 
   if (warp == 0) {
-    // ───────────── TMA producer ─────────────
-    if (lane == 0) {
-      uint32_t it = 0;
-      bool alive = true;
-      for (int tile = blockIdx.x; tile < ntiles && alive; tile += gridDim.x) {
-        const int4 td = args.tiles[tile];
-        const int set = td.z >> 24, e = td.z & 0xFFFFFF;
-        const int arow = e * args.a_expert_rows[set] + td.w * 128;
-        for (int kb = 0; kb < nkb; ++kb) {
-          const int s = it % NSTAGE;
-          const uint32_t ph = (it / NSTAGE) & 1;
-          if (!mbar_wait(&empty[s], ph ^ 1, s_abort)) {
-            alive = false;
-            break;
-          }
+    // ───────────── TMA producer (lane 0) + scale staging (all lanes, cp.async) ─────────────
+    uint32_t it = 0;
+    bool alive = true;
+    for (int tile = blockIdx.x; tile < ntiles && alive; tile += gridDim.x) {
+      const int4 td = args.tiles[tile];
+      const int set = td.z >> 24, e = td.z & 0xFFFFFF;
+      const int nr = td.y;
+      const int arow = e * args.a_expert_rows[set] + td.w * 128;
+      const float* wsp = args.ws[set][lane < NACC ? lane : 0] + e * args.ws_expert_stride[set] + td.w * args.ws_nb_stride;
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = it % NSTAGE;
+        const uint32_t ph = (it / NSTAGE) & 1;
+        const int j = it % C::NSLOT;
+        const uint32_t jph = (it / C::NSLOT) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1, s_abort) || !mbar_wait(&sfree[j], jph ^ 1, s_abort)) {
+          alive = false;
+          break;
+        }
+        if (lane == 0) {
           uint8_t* st = smem + s * C::STAGE_BYTES;
           mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
 #pragma unroll
           for (int a = 0; a < NACC; ++a) tma_load_2d(st + a * C::A_BYTES, &args.tmA[set][a], &full[s], kb * 128, arow);
           tma_load_2d(st + NACC * C::A_BYTES, &args.tmB, &full[s], kb * 128, td.x);
-          ++it;
         }
+        float* slot = slots + j * C::SLOT_FLOATS;
+#pragma unroll
+        for (int u = 0; u < BN / 32; ++u) {
+          const int r = lane + 32 * u;
+          if (r < nr) cp_async_4(slot + r, args.as + (int64_t)(td.x + r) * args.as_row + (int64_t)kb * args.as_kb);
+        }
+        if (lane < NACC) cp_async_4(slot + BN + lane, wsp + kb);
+        cp_async_mbar_arrive(&sready[j]);
+        ++it;
       }
-      // no bulk copy into this CTA's shared memory may outlive the CTA
-      const uint32_t first = it > (uint32_t)NSTAGE ? it - NSTAGE : 0;
-      for (uint32_t j = first; j < it; ++j) wait_plain(&full[j % NSTAGE], (j / NSTAGE) & 1, kWaitTimeoutNs);
     }
-  } else if (warp == 1) {
-    // ───────────── MMA issuer + scale staging ─────────────
+    cp_async_wait_all();
+    // no copy into this CTA's shared memory may outlive the CTA
+    if (lane == 0) {
+      const uint32_t first = it > (uint32_t)NSTAGE ? it - NSTAGE : 0;
+      for (uint32_t q = first; q < it; ++q) wait_plain(&full[q % NSTAGE], (q / NSTAGE) & 1, kWaitTimeoutNs);
+    }
+    __syncwarp();
+  } else if (warp >= 1 && warp <= C::NISSUE) {
+    // ───────────── MMA issuers: warp 1+i takes K-block steps it % NISSUE == i ─────────────
+    // A single thread sustains about one tcgen05.mma per 67 cycles, so two issuers keep the
+    // tensor core fed at small N.  Every K-block step has its own stage and TMEM buffer, so the
+    // issuers never touch the same accumulator and results do not depend on their interleaving.
+    const int me = warp - 1;
     uint32_t it = 0, ait = 0;
     bool alive = true;
     for (int tile = blockIdx.x; tile < ntiles && alive; tile += gridDim.x) {
@@ -169,31 +204,18 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
       int n_eff = (nr + 15) & ~15;
       n_eff = n_eff < 16 ? 16 : (n_eff > BN ? BN : n_eff);
       const uint32_t idesc = umma_idesc_e4m3(128, n_eff);
-      const float* ws0 = args.ws[set][0] + e * args.ws_expert_stride[set] + td.w * args.ws_nb_stride;
-      const float* ws1 = NACC > 1 ? args.ws[set][NACC - 1] + e * args.ws_expert_stride[set] + td.w * args.ws_nb_stride
-                                  : ws0;
       for (int kb = 0; kb < nkb; ++kb) {
-        float asv[BN / 32];
-#pragma unroll
-        for (int j = 0; j < BN / 32; ++j) {
-          const int r = lane + 32 * j;
-          asv[j] = r < nr ? __ldg(args.as + (int64_t)(td.x + r) * args.as_row + (int64_t)kb * args.as_kb) : 0.f;
+        if ((int)(it % C::NISSUE) != me) {
+          ++it;
+          ++ait;
+          continue;
         }
-        const float wsv = lane == 0 ? __ldg(ws0 + kb) : (lane == 1 ? __ldg(ws1 + kb) : 0.f);
         const int b = ait % NBUF;
         const uint32_t aph = (ait / NBUF) & 1;
         if (!mbar_wait(&acce[b], aph ^ 1, s_abort)) {
           alive = false;
           break;
         }
-#pragma unroll
-        for (int a = 0; a < NACC; ++a) {
-          const float w = __shfl_sync(0xffffffffu, wsv, a);
-#pragma unroll
-          for (int j = 0; j < BN / 32; ++j) scl[(b * NACC + a) * BN + lane + 32 * j] = asv[j] * w;
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&accf[b]);
         const int s = it % NSTAGE;
         const uint32_t ph = (it / NSTAGE) & 1;
         if (!mbar_wait(&full[s], ph, s_abort)) {
@@ -204,13 +226,15 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
         if (lane == 0) {
           uint8_t* st = smem + s * C::STAGE_BYTES;
           const uint64_t bdesc = umma_desc_sw128(smem_u32(st + NACC * C::A_BYTES));
+          uint64_t adesc[NACC];
+#pragma unroll
+          for (int a = 0; a < NACC; ++a) adesc[a] = umma_desc_sw128(smem_u32(st + a * C::A_BYTES));
+          const uint32_t d0 = tmem + (uint32_t)(b * NACC * BN);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
 #pragma unroll
-            for (int a = 0; a < NACC; ++a) {
-              const uint64_t adesc = umma_desc_sw128(smem_u32(st + a * C::A_BYTES));
-              umma_f8(tmem + (uint32_t)((b * NACC + a) * BN), adesc + 2 * kk, bdesc + 2 * kk, idesc, kk > 0 ? 1u : 0u);
-            }
+            for (int a = 0; a < NACC; ++a)
+              umma_f8(d0 + (uint32_t)(a * BN), adesc[a] + 2 * kk, bdesc + 2 * kk, idesc, kk > 0 ? 1u : 0u);
           }
           umma_commit(&empty[s]);
           umma_commit(&accf[b]);
@@ -222,8 +246,8 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
     }
     // every MMA must have completed before TMEM is released
     if (lane == 0) {
-      umma_commit(drain);
-      wait_plain(drain, 0, kWaitTimeoutNs);
+      umma_commit(&drain[me]);
+      wait_plain(&drain[me], 0, kWaitTimeoutNs);
     }
     __syncwarp();
   } else if (warp >= 4) {
@@ -259,30 +283,59 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
           break;
         }
         tc_fence_after();
+        // this K block's scales: a_scale per column (token row) and w_scale per accumulator
+        const int j = ait % C::NSLOT;
+        if (!mbar_wait(&sready[j], (ait / C::NSLOT) & 1, s_abort)) {
+          alive = false;
+          break;
+        }
+        const float* slot = slots + j * C::SLOT_FLOATS;
+        // 32 columns per TMEM load; the buffer is handed back to the MMA warps as soon as the
+        // last load of this K block has landed
+        // 32-column groups of this warpgroup's slice that hold real columns
+        const int span = n_eff - wg * CW;
+        const int ngroups = span <= 0 ? 0 : (span >= CW ? CW / 32 : (span + 31) / 32);
+        if (ngroups == 0) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acce[b]);
+        }
 #pragma unroll
         for (int a = 0; a < NACC; ++a) {
 #pragma unroll
-          for (int cc = 0; cc < CW / 16; ++cc) {
-            const int col = wg * CW + cc * 16;
-            if (col < n_eff) {
-              float pv[16];
-              tmem_ld16(tmem + tlane + (uint32_t)((b * NACC + a) * BN + col), pv);
+          for (int g = 0; g < CW / 32; ++g) {
+            const int col = wg * CW + g * 32;
+            const bool last = (a == NACC - 1) && (g == ngroups - 1);
+            if (g < ngroups) {
+              float pv[32];
+              const uint32_t ta = tmem + tlane + (uint32_t)((b * NACC + a) * BN + col);
+              if (col + 32 <= n_eff) tmem_ld32(ta, pv);
+              else tmem_ld16p(ta, pv);
               tmem_ld_wait();
-              const float4* sc4 = reinterpret_cast<const float4*>(scl + (b * NACC + a) * BN + col);
+              if (last) {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acce[b]);
+              }
+              const float wsa = slot[BN + a];
+              const float4* sc4 = reinterpret_cast<const float4*>(slot + col);
 #pragma unroll
-              for (int i4 = 0; i4 < 4; ++i4) {
-                const float4 s4 = sc4[i4];
-                acc[a][cc * 16 + i4 * 4 + 0] = fmaf(pv[i4 * 4 + 0], s4.x, acc[a][cc * 16 + i4 * 4 + 0]);
-                acc[a][cc * 16 + i4 * 4 + 1] = fmaf(pv[i4 * 4 + 1], s4.y, acc[a][cc * 16 + i4 * 4 + 1]);
-                acc[a][cc * 16 + i4 * 4 + 2] = fmaf(pv[i4 * 4 + 2], s4.z, acc[a][cc * 16 + i4 * 4 + 2]);
-                acc[a][cc * 16 + i4 * 4 + 3] = fmaf(pv[i4 * 4 + 3], s4.w, acc[a][cc * 16 + i4 * 4 + 3]);
+              for (int i4 = 0; i4 < 8; ++i4) {
+                float4 s4 = sc4[i4];
+                s4.x *= wsa;
+                s4.y *= wsa;
+                s4.z *= wsa;
+                s4.w *= wsa;
+                acc[a][g * 32 + i4 * 4 + 0] = fmaf(pv[i4 * 4 + 0], s4.x, acc[a][g * 32 + i4 * 4 + 0]);
+                acc[a][g * 32 + i4 * 4 + 1] = fmaf(pv[i4 * 4 + 1], s4.y, acc[a][g * 32 + i4 * 4 + 1]);
+                acc[a][g * 32 + i4 * 4 + 2] = fmaf(pv[i4 * 4 + 2], s4.z, acc[a][g * 32 + i4 * 4 + 2]);
+                acc[a][g * 32 + i4 * 4 + 3] = fmaf(pv[i4 * 4 + 3], s4.w, acc[a][g * 32 + i4 * 4 + 3]);
               }
             }
           }
         }
-        tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&acce[b]);
+        if (lane == 0) mbar_arrive(&sfree[j]);
         ++ait;
       }
       if (!alive) break;
@@ -293,7 +346,8 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
 #pragma unroll
         for (int c = 0; c < CW; ++c) {
           const int t = wg * CW + c;
-          if (t < nr) out[(row0 + t) * args.out_ld + ncol] = __float2bfloat16_rn(acc[0][c]);
+          if (t >= nr) break;
+          out[(row0 + t) * args.out_ld + ncol] = __float2bfloat16_rn(acc[0][c]);
         }
       } else {
         // SwiGLU exactly as the reference rounds it: gate/up GEMM outputs are bf16
@@ -301,6 +355,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
         // then _fast_fp8_quantize over these 128 channels (:637).
 #pragma unroll
         for (int c = 0; c < CW; ++c) {
+          if (wg * CW + c >= nr) break;  // warp-uniform
           const float g = bf16_round(acc[0][c]);
           const float u = bf16_round(acc[NACC - 1][c]);
           const float sl = bf16_round(__fdiv_rn(g, 1.0f + expf(-g)));
@@ -314,14 +369,13 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
 #pragma unroll
         for (int c = 0; c < CW; ++c) {
           const int t = wg * CW + c;
+          if (t >= nr) break;
           const float* rr = red + wg * 4 * CW + c;
           const float am = nanmax(nanmax(rr[0], rr[CW]), nanmax(rr[2 * CW], rr[3 * CW]));
           const float s = (am != am) ? am : __fdiv_rn(fmaxf(am, 1e-12f), 448.0f);
-          if (t < nr) {
-            const float qv = clamp_pm(__fdiv_rn(acc[0][c], s), 448.0f);
-            outq[(row0 + t) * args.out_ld + ncol] = (uint8_t)(f32x2_to_e4m3x2(qv, 0.f) & 0xFF);
-            if (lrow == 0) args.out_scale[(row0 + t) * args.os_row + (int64_t)td.w * args.os_kb] = s;
-          }
+          const float qv = clamp_pm(__fdiv_rn(acc[0][c], s), 448.0f);
+          outq[(row0 + t) * args.out_ld + ncol] = (uint8_t)(f32x2_to_e4m3x2(qv, 0.f) & 0xFF);
+          if (lrow == 0) args.out_scale[(row0 + t) * args.os_row + (int64_t)td.w * args.os_kb] = s;
         }
         if (!wg_sync()) break;
       }

@@ -44,44 +44,52 @@ __global__ void __launch_bounds__(kQuantWarps * 32) k_quant_rows(QuantArgs a) {
   } else {
     src = r - a.rows_a;
   }
-  const __nv_bfloat16* xr = a.x + src * a.ldx;
-  uint8_t* qr = a.q + (int64_t)r * a.ldq;
+  const __nv_bfloat16* __restrict__ xr = a.x + src * a.ldx;
+  uint8_t* __restrict__ qr = a.q + (int64_t)r * a.ldq;
   float dot = 0.f;
   const bool want_gate = seg_b && a.gate_w != nullptr;
-  for (int c0 = 0; c0 < a.K; c0 += 256) {
-    const int c = c0 + lane * 8;
-    float f[8];
-    uint4 raw = make_uint4(0, 0, 0, 0);
-    if (c < a.K) raw = *reinterpret_cast<const uint4*>(xr + c);
-    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw);
-    float am = 0.f;
+  constexpr int kBatch = 4;  // 256-channel slabs loaded before any is processed
+  for (int c0 = 0; c0 < a.K; c0 += 256 * kBatch) {
+    uint4 raw[kBatch];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      f[i] = __bfloat162float(h[i]);
-      am = nanmax(am, fabsf(f[i]));
-    }
-    if (want_gate && c < a.K) {
-      uint4 wraw = *reinterpret_cast<const uint4*>(a.gate_w + c);
-      const __nv_bfloat16* wh = reinterpret_cast<const __nv_bfloat16*>(&wraw);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) dot = fmaf(f[i], __bfloat162float(wh[i]), dot);
+    for (int b = 0; b < kBatch; ++b) {
+      const int c = c0 + b * 256 + lane * 8;
+      raw[b] = c < a.K ? *reinterpret_cast<const uint4*>(xr + c) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) am = nanmax(am, __shfl_xor_sync(0xffffffffu, am, o));
-    // s = clamp(amax, min=1e-12) / 448 (NaN propagates as in torch.clamp)
-    const float s = (am != am) ? am : __fdiv_rn(fmaxf(am, 1e-12f), 448.0f);
-    if (c < a.K) {
-      uint32_t packed[2];
+    for (int b = 0; b < kBatch; ++b) {
+      const int c = c0 + b * 256 + lane * 8;
+      float f[8];
+      const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw[b]);
+      float am = 0.f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float lo = clamp_pm(__fdiv_rn(f[2 * i], s), 448.0f);
-        float hi = clamp_pm(__fdiv_rn(f[2 * i + 1], s), 448.0f);
-        uint16_t pr = f32x2_to_e4m3x2(lo, hi);
-        if (i & 1) packed[i >> 1] |= (uint32_t)pr << 16;
-        else packed[i >> 1] = pr;
+      for (int i = 0; i < 8; ++i) {
+        f[i] = __bfloat162float(h[i]);
+        am = nanmax(am, fabsf(f[i]));
       }
-      *reinterpret_cast<uint2*>(qr + c) = make_uint2(packed[0], packed[1]);
-      if ((lane & 15) == 0) a.scale[(int64_t)r * a.s_row + (int64_t)(c / 128) * a.s_kb] = s;
+      if (want_gate && c < a.K) {
+        uint4 wraw = *reinterpret_cast<const uint4*>(a.gate_w + c);
+        const __nv_bfloat16* wh = reinterpret_cast<const __nv_bfloat16*>(&wraw);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dot = fmaf(f[i], __bfloat162float(wh[i]), dot);
+      }
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) am = nanmax(am, __shfl_xor_sync(0xffffffffu, am, o));
+      // s = clamp(amax, min=1e-12) / 448 (NaN propagates as in torch.clamp)
+      const float s = (am != am) ? am : __fdiv_rn(fmaxf(am, 1e-12f), 448.0f);
+      if (c < a.K) {
+        uint32_t packed[2];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float lo = clamp_pm(__fdiv_rn(f[2 * i], s), 448.0f);
+          float hi = clamp_pm(__fdiv_rn(f[2 * i + 1], s), 448.0f);
+          uint16_t pr = f32x2_to_e4m3x2(lo, hi);
+          if (i & 1) packed[i >> 1] |= (uint32_t)pr << 16;
+          else packed[i >> 1] = pr;
+        }
+        *reinterpret_cast<uint2*>(qr + c) = make_uint2(packed[0], packed[1]);
+        if ((lane & 15) == 0) a.scale[(int64_t)r * a.s_row + (int64_t)(c / 128) * a.s_kb] = s;
+      }
     }
   }
   if (want_gate) {
@@ -113,43 +121,35 @@ struct CombineArgs {
 
 constexpr int kCombineThreads = 256;
 
-// One CTA per token; each thread produces 8 consecutive channels per pass.
+// One CTA per token; each thread produces 8 consecutive channels per pass.  Warp 0 reads
+// the token's k slots in parallel (and orders them by expert id for the per-expert modes);
+// the channel loop keeps 4 slot rows in flight at a time.
 __global__ void __launch_bounds__(kCombineThreads) k_combine(CombineArgs a) {
   const int t = blockIdx.x;
   __shared__ int s_row[16];
   __shared__ float s_w[16];
-  if (threadIdx.x == 0) {
-    int rows[16], ids[16];
-    float ws[16];
-    int n = 0;
-    for (int j = 0; j < a.k; ++j) {
-      int r = a.slot_row[(int64_t)t * a.k + j];
-      float w = a.w_f32 ? reinterpret_cast<const float*>(a.topk_w)[(int64_t)t * a.k + j]
-                        : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.topk_w)[(int64_t)t * a.k + j]);
-      rows[n] = r;
-      ws[n] = w;
-      ids[n] = a.topk_ids ? a.topk_ids[(int64_t)t * a.k + j] : j;
-      ++n;
+  if (threadIdx.x < 32) {
+    const int j = threadIdx.x;
+    int r = -1, id = 0x7fffffff;
+    float w = 0.f;
+    if (j < a.k) {
+      const int64_t o = (int64_t)t * a.k + j;
+      r = a.slot_row[o];
+      w = a.w_f32 ? reinterpret_cast<const float*>(a.topk_w)[o]
+                  : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.topk_w)[o]);
+      id = a.topk_ids ? a.topk_ids[o] : j;
     }
+    int pos = j;
     if (a.mode != MSV_COMBINE_V2) {  // expert-ascending order of the per-expert loops
-      for (int i = 1; i < n; ++i) {
-        int r = rows[i], id = ids[i];
-        float w = ws[i];
-        int j = i - 1;
-        while (j >= 0 && ids[j] > id) {
-          rows[j + 1] = rows[j];
-          ws[j + 1] = ws[j];
-          ids[j + 1] = ids[j];
-          --j;
-        }
-        rows[j + 1] = r;
-        ws[j + 1] = w;
-        ids[j + 1] = id;
+      pos = 0;
+      for (int i = 0; i < a.k; ++i) {
+        const int idi = __shfl_sync(0xffffffffu, id, i);
+        pos += (idi < id) || (idi == id && i < j);
       }
     }
-    for (int j = 0; j < n; ++j) {
-      s_row[j] = rows[j];
-      s_w[j] = ws[j];
+    if (j < a.k) {
+      s_row[pos] = r;
+      s_w[pos] = w;
     }
   }
   __syncthreads();
@@ -158,19 +158,28 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(CombineArgs a) {
     float acc[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-    for (int j = 0; j < a.k; ++j) {
-      const int r = s_row[j];
-      if (r < 0) continue;
-      const float w = s_w[j];
-      uint4 raw = *reinterpret_cast<const uint4*>(a.down + (int64_t)r * a.ld_down + c);
-      const __nv_bfloat16* d = reinterpret_cast<const __nv_bfloat16*>(&raw);
+    for (int j0 = 0; j0 < a.k; j0 += 4) {
+      uint4 raw[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float dv = __bfloat162float(d[i]);
-        if (a.mode == MSV_COMBINE_V2) acc[i] += bf16_round(dv * w);
-        // fp32 product and fp32 add rounded separately (no FMA contraction), then bf16
-        else if (a.mode == MSV_COMBINE_DISPATCH) acc[i] = bf16_round(__fadd_rn(acc[i], __fmul_rn(dv, w)));
-        else acc[i] = bf16_round(acc[i] + bf16_round(dv * w));
+      for (int u = 0; u < 4; ++u) {
+        const int r = (j0 + u < a.k) ? s_row[j0 + u] : -1;
+        raw[u] = r >= 0 ? *reinterpret_cast<const uint4*>(a.down + (int64_t)r * a.ld_down + c) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = j0 + u;
+        if (j >= a.k) break;
+        if (s_row[j] < 0) continue;
+        const float w = s_w[j];
+        const __nv_bfloat16* d = reinterpret_cast<const __nv_bfloat16*>(&raw[u]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float dv = __bfloat162float(d[i]);
+          if (a.mode == MSV_COMBINE_V2) acc[i] += bf16_round(dv * w);
+          // fp32 product and fp32 add rounded separately (no FMA contraction), then bf16
+          else if (a.mode == MSV_COMBINE_DISPATCH) acc[i] = bf16_round(__fadd_rn(acc[i], __fmul_rn(dv, w)));
+          else acc[i] = bf16_round(acc[i] + bf16_round(dv * w));
+        }
       }
     }
     if (a.add_shared) {

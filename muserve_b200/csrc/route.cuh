@@ -342,29 +342,51 @@ MSV_DEVICE int load_id(const PermuteArgs& p, int f) {
   return p.ids_i64 ? (int)reinterpret_cast<const int64_t*>(p.ids)[f] : reinterpret_cast<const int32_t*>(p.ids)[f];
 }
 
+// Block-wide exclusive scan of one int per thread (1024 threads); *total gets the sum.
+// s_warp needs 33 ints.  Contains __syncthreads: every thread of the block must call it.
+MSV_DEVICE int block_excl_scan(int v, int* s_warp, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int w = s_warp[lane];
+    int wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += y;
+    }
+    s_warp[lane] = wi - w;
+    if (lane == 31) s_warp[32] = wi;
+  }
+  __syncthreads();
+  const int excl = s_warp[warp] + incl - v;
+  *total = s_warp[32];
+  __syncthreads();
+  return excl;
+}
+
 // Tile list of one grouped GEMM: per local expert with c rows, ceil(c/bn) row chunks of
 // near-equal size (multiples of 16) times nb weight n-blocks, ordered expert, n-block, chunk
 // (chunks sharing a weight tile are adjacent).  The shared-expert group goes first.
-MSV_DEVICE void build_tiles(const PermuteArgs& p, const int* counts, const int* offsets, int* scratch, int4* tiles,
-                            int* ntiles, int bn, int nb) {
+MSV_DEVICE void build_tiles(const PermuteArgs& p, const int* counts, const int* offsets, int* scratch, int* s_warp,
+                            int4* tiles, int* ntiles, int bn, int nb) {
   const int tid = threadIdx.x;
   const int nsh_chunks = p.shared_rows > 0 ? (p.shared_rows + bn - 1) / bn : 0;
   const int nsh = nsh_chunks * nb;
-  // per-expert tile counts, exclusive scan (sequential per 1024-chunk is enough: e_local <= 1024)
-  for (int e = tid; e < p.e_local; e += kPermThreads) {
-    int c = counts[e];
-    scratch[e] = c > 0 ? ((c + bn - 1) / bn) * nb : 0;
-  }
-  __syncthreads();
-  if (tid == 0) {
-    int run = nsh;
-    for (int e = 0; e < p.e_local; ++e) {
-      int n = scratch[e];
-      scratch[e] = run;
-      run += n;
-    }
-    *ntiles = run;
-  }
+  // per-expert tile counts -> exclusive scan (one expert per thread, e_local <= 1024)
+  const int c_mine = tid < p.e_local ? counts[tid] : 0;
+  const int n_mine = c_mine > 0 ? ((c_mine + bn - 1) / bn) * nb : 0;
+  int total = 0;
+  const int base_mine = block_excl_scan(n_mine, s_warp, &total);
+  if (tid < p.e_local) scratch[tid] = nsh + base_mine;
+  if (tid == 0) *ntiles = nsh + total;
   __syncthreads();
   // shared-expert tiles
   for (int i = tid; i < nsh; i += kPermThreads) {
@@ -399,6 +421,7 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermuteArgs p) {
   extern __shared__ __align__(16) int hist[];  // [kPermWarps][e_local], then scratch
   __shared__ int s_nloc[kPermWarps];
   __shared__ int s_total;
+  __shared__ int s_warp[33];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int E = p.e_local;
   int* counts = hist + kPermWarps * E;   // [E]
@@ -429,15 +452,15 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermuteArgs p) {
     counts[e] = c;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int run = 0;
-    for (int e = 0; e < E; ++e) {
-      offsets[e] = run;
-      run += counts[e];
+  {
+    int total = 0;
+    const int off = block_excl_scan(threadIdx.x < E ? counts[threadIdx.x] : 0, s_warp, &total);
+    if (threadIdx.x < E) offsets[threadIdx.x] = off;
+    if (threadIdx.x == 0) {
+      offsets[E] = total;
+      s_total = total;
+      *p.num_local = total;
     }
-    offsets[E] = run;
-    s_total = run;
-    *p.num_local = run;
   }
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += kPermThreads) {
@@ -484,8 +507,8 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermuteArgs p) {
     const int padded = ((nl + p.alignment - 1) / p.alignment) * p.alignment;
     for (int r = nl + threadIdx.x; r < padded; r += kPermThreads) p.sorted_expert_ids[r] = -1;
   }
-  if (p.tiles1) build_tiles(p, counts, offsets, scratch, p.tiles1, p.ntiles1, p.bn1, p.nb1);
-  if (p.tiles2) build_tiles(p, counts, offsets, scratch, p.tiles2, p.ntiles2, p.bn2, p.nb2);
+  if (p.tiles1) build_tiles(p, counts, offsets, scratch, s_warp, p.tiles1, p.ntiles1, p.bn1, p.nb1);
+  if (p.tiles2) build_tiles(p, counts, offsets, scratch, s_warp, p.tiles2, p.ntiles2, p.bn2, p.nb2);
 }
 
 size_t permute_smem_bytes(int e_local) { return (size_t)(kPermWarps * e_local + 3 * e_local + 1) * sizeof(int); }

@@ -45,8 +45,12 @@ def test_quant_special_values(cuda):
     q, s = moe.fp8_quant_128(x.to(cuda))
     rq, rs = orc.fast_fp8_quantize(x)
     assert torch.equal(s.cpu().isnan(), rs.isnan())
-    fin = ~rs.isnan().repeat_interleave(128, 1)
-    assert torch.equal(q.cpu().view(torch.uint8)[fin], rq.view(torch.uint8)[fin])
+    # invalid operations (inf/inf) give a NaN whose sign is platform-defined (x86: negative
+    # default NaN -> e4m3 0xFF; GPU: 0x7F): compare NaN-ness there, bytes everywhere else
+    qb, rb = q.cpu().view(torch.uint8), rq.view(torch.uint8)
+    rnan = (rb & 0x7F) == 0x7F
+    assert torch.equal((qb & 0x7F) == 0x7F, rnan)
+    assert torch.equal(qb[~rnan], rb[~rnan])
 
 
 def test_quant_gather_and_kb_major(cuda):
