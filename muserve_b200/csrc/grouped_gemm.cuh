@@ -11,17 +11,25 @@
 // HBM once per token chunk.  A tile = (group, n-block, token chunk); the tile list is built
 // on the device, the kernel is persistent (one CTA per SM, static round robin over tiles).
 //
+// The 128x128 fp32 weight scales and per-row x 128 activation scales are arbitrary fp32
+// values, so they cannot be folded into a UE8M0 block-scaled MMA: every 128-wide K block
+// ("K step") is accumulated into its own TMEM buffer and promoted into fp32 registers with
+// its scale (as the reference's block-wise scaling defines it).
+//
 // Roles (warp-specialised, one CTA per SM):
-//   warp 0      TMA producer: per 128-wide K block, NACC weight boxes [128 x 128 B] and one
-//               token box [BN x 128 B], 128-byte swizzle, into an NSTAGE ring.
-//   warp 1      MMA issuer: tcgen05.mma kind::f8f6f4 (e4m3 x e4m3 -> fp32), 4 x K=32 per K
-//               block, into a fresh TMEM buffer per K block (NBUF-deep ring); also stages the
-//               K block's scales (a_scale[row] * w_scale) in shared memory; owns TMEM alloc.
-//   warps 4..   epilogue warpgroups: per K block, tcgen05.ld the partial product, multiply by
-//               the staged scales and accumulate in fp32 registers (the 128x128 fp32 scales
-//               are arbitrary, so the scale cannot be folded into a UE8M0 block-scaled MMA);
-//               at tile end write bf16 (EPI 0), or SwiGLU + per-128 e4m3 requant (EPI 1:
-//               acc 0 = gate rows, acc 1 = up rows of the same 128 channels).
+//   warp 0      TMA producer: per K step, NACC weight boxes [128 x 128 B] and one token box
+//               [BN x 128 B] (128-byte swizzle) into an NSTAGE ring; its 32 lanes also copy
+//               the step's activation and weight scales into a scale-slot ring (cp.async).
+//   warps 1, 2  MMA issuers, alternate K steps: tcgen05.mma kind::f8f6f4 (e4m3 x e4m3 -> fp32),
+//               4 x K=32 per step per accumulator, into the step's TMEM buffer (NBUF ring).
+//               A single thread issues about one MMA per 67 cycles, so two share the work;
+//               every step has its own stage and buffer, so the order they run in is free.
+//   warp 3      scale warp: per K step, combined scale a_scale[row] * w_scale[acc] for every
+//               column of the tile, computed once into shared memory.
+//   warps 4..   epilogue warpgroups: per K step, tcgen05.ld 32 columns at a time, hand the
+//               TMEM buffer back as soon as the last load landed, then acc += partial * scale
+//               with paired fp32 FMAs.  At tile end: bf16 out (EPI 0), or SwiGLU + per-128
+//               e4m3 requant (EPI 1: acc 0 = gate rows, acc 1 = up rows of the same channels).
 // Every wait is bounded (common.cuh); on timeout the CTA drains its copies and MMAs, frees
 // TMEM and raises MSV_ERR_TIMEOUT in the error word.
 #pragma once
@@ -61,29 +69,26 @@ struct GemmCfg {
                                    : COLS_USED <= 256 ? 256 : 512;
   static constexpr int CW = BN / NWG;
   static constexpr int THREADS = 128 + 128 * NWG;
-  static constexpr int SCL_BYTES = 0;
+  static constexpr int NISSUE = 2;
+  static constexpr int NSLOT = 8;                       // scale-slot ring depth (K steps)
+  static constexpr int RAW_FLOATS = BN + 4;             // per slot: a_scale of the chunk's rows, w_scale per acc
+  static constexpr int SCL_FLOATS = NACC * BN;          // per slot: combined scales
   static constexpr int RED_BYTES = EPI == 1 ? NWG * 4 * CW * 4 : 0;
-  static constexpr int SLOT_FLOATS = BN + 4;  // per K-block step: a_scale of the chunk's rows, then w_scale per acc
-  static constexpr int NSLOT_MAX = 20;
-  static constexpr int TAIL_BYTES = SCL_BYTES + RED_BYTES + 128 * 8 + 64 + NSLOT_MAX * SLOT_FLOATS * 4;
+  static constexpr int TAIL_BYTES = NSLOT * (RAW_FLOATS + SCL_FLOATS) * 4 + RED_BYTES + 128 * 8 + 64;
   static constexpr int SMEM_LIMIT = 232448 - 1024;  // 227 KB opt-in, minus alignment slack
   static constexpr int NSTAGE_RAW = (SMEM_LIMIT - TAIL_BYTES) / STAGE_BYTES;
   static constexpr int NSTAGE = NSTAGE_RAW > 12 ? 12 : NSTAGE_RAW;
-  static constexpr int OFF_SCL = NSTAGE * STAGE_BYTES;
-  static constexpr int OFF_RED = OFF_SCL + SCL_BYTES;
-  // scale slots outlive their smem stage (the epilogue reads them after the MMA released the
-  // stage), so they form their own ring with ready/free barriers
-  static constexpr int NSLOT = NSTAGE + NBUF + 2 <= NSLOT_MAX ? NSTAGE + NBUF + 2 : NSLOT_MAX;
-  static constexpr int OFF_SLOT = OFF_RED + RED_BYTES;
-  static constexpr int OFF_BAR = (OFF_SLOT + NSLOT * SLOT_FLOATS * 4 + 7) & ~7;
-  static constexpr int NISSUE = 2;  // MMA-issuing warps (1, 2), taking alternate K blocks
-  static constexpr int NBARS = 2 * NSTAGE + 2 * NBUF + NISSUE + NWG + 2 * NSLOT;
+  static constexpr int OFF_RAW = NSTAGE * STAGE_BYTES;
+  static constexpr int OFF_SCL = OFF_RAW + NSLOT * RAW_FLOATS * 4;
+  static constexpr int OFF_RED = OFF_SCL + NSLOT * SCL_FLOATS * 4;
+  static constexpr int OFF_BAR = (OFF_RED + RED_BYTES + 7) & ~7;
+  static constexpr int NBARS = 2 * NSTAGE + 2 * NBUF + NISSUE + NWG + 3 * NSLOT;
   static constexpr int OFF_MISC = OFF_BAR + NBARS * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   static_assert(CW % 32 == 0, "column slice must be whole 32-column TMEM loads");
   static_assert(NBUF >= 2, "need at least double-buffered TMEM partials");
   static_assert(NSTAGE >= 2, "pipeline too shallow");
-  static_assert(NSLOT > NSTAGE + NBUF, "scale ring must outlast the stage ring plus the TMEM ring");
+  static_assert(NBARS <= 128, "barrier area");
   static_assert(SMEM_BYTES <= 232448, "shared memory over the sm_100 limit");
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
 };
@@ -95,41 +100,66 @@ MSV_DEVICE bool wait_plain(uint64_t* bar, uint32_t parity, unsigned long long li
   return true;
 }
 
+// Ring position: index and phase parity advanced without division.
+template <int N>
+struct Ring {
+  int i = 0;
+  uint32_t ph = 0;
+  MSV_DEVICE void next() {
+    if (++i == N) {
+      i = 0;
+      ph ^= 1;
+    }
+  }
+};
+
+// acc[0..1] += p[0..1] * s[0..1] as one paired fp32 FMA.
+MSV_DEVICE void fma2(float& a0, float& a1, float p0, float p1, float s0, float s1) {
+  uint64_t a, p, s, d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(p) : "f"(p0), "f"(p1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(s) : "f"(s0), "f"(s1));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(p), "l"(s), "l"(a));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a0), "=f"(a1) : "l"(d));
+}
+
 template <class C>
 __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_constant__ GemmArgs args) {
-  constexpr int BN = C::BN, NACC = C::NACC, NSTAGE = C::NSTAGE, NBUF = C::NBUF, CW = C::CW;
+  constexpr int BN = C::BN, NACC = C::NACC, NSTAGE = C::NSTAGE, NBUF = C::NBUF, CW = C::CW, NSLOT = C::NSLOT;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* raw = reinterpret_cast<float*>(smem + C::OFF_RAW);
   float* scl = reinterpret_cast<float*>(smem + C::OFF_SCL);
   float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
-  float* slots = reinterpret_cast<float*>(smem + C::OFF_SLOT);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* empty = full + NSTAGE;
   uint64_t* accf = empty + NSTAGE;
   uint64_t* acce = accf + NBUF;
-  uint64_t* drain = acce + NBUF;      // one per issuing warp
-  uint64_t* epib = drain + C::NISSUE;  // per epilogue warpgroup: 4 warps meet here (bounded)
-  uint64_t* sready = epib + C::NWG;    // scale slot landed (one cp.async arrival per producer lane)
-  uint64_t* sfree = sready + C::NSLOT; // scale slot consumed (one arrival per epilogue warp)
+  uint64_t* drain = acce + NBUF;         // one per issuing warp
+  uint64_t* epib = drain + C::NISSUE;    // per epilogue warpgroup: 4 warps meet here (bounded)
+  uint64_t* sready = epib + C::NWG;      // raw scales landed (one cp.async arrival per producer lane)
+  uint64_t* cready = sready + NSLOT;     // combined scales written by the scale warp
+  uint64_t* sfree = cready + NSLOT;      // slot consumed (one arrival per epilogue warp)
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < NSTAGE; ++s) {
-      mbar_init(&full[s], 1);  // TMA expect_tx
+      mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < NBUF; ++b) {
-      mbar_init(&accf[b], 1);           // MMA commit
-      mbar_init(&acce[b], 4 * C::NWG);  // one arrive per epilogue warp
-    }
-    for (int j = 0; j < C::NSLOT; ++j) {
-      mbar_init(&sready[j], 32);
-      mbar_init(&sfree[j], 4 * C::NWG);
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 4 * C::NWG);
     }
     for (int i = 0; i < C::NISSUE; ++i) mbar_init(&drain[i], 1);
     for (int g = 0; g < C::NWG; ++g) mbar_init(&epib[g], 4);
+    for (int j = 0; j < NSLOT; ++j) {
+      mbar_init(&sready[j], 32);
+      mbar_init(&cready[j], 1);
+      mbar_init(&sfree[j], 4 * C::NWG);
+    }
     *s_abort = 0;
     fence_mbar_init();
   }
@@ -146,8 +176,10 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
   const int nkb = args.num_kb;
 
   if (warp == 0) {
-    // ───────────── TMA producer (lane 0) + scale staging (all lanes, cp.async) ─────────────
-    uint32_t it = 0;
+    // ───────────── TMA producer (lane 0) + raw scale copies (all lanes) ─────────────
+    Ring<NSTAGE> st;
+    Ring<NSLOT> sl;
+    uint32_t issued = 0;
     bool alive = true;
     for (int tile = blockIdx.x; tile < ntiles && alive; tile += gridDim.x) {
       const int4 td = args.tiles[tile];
@@ -155,93 +187,75 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
       const int nr = td.y;
       const int arow = e * args.a_expert_rows[set] + td.w * 128;
       const float* wsp = args.ws[set][lane < NACC ? lane : 0] + e * args.ws_expert_stride[set] + td.w * args.ws_nb_stride;
+      const float* asp = args.as + (int64_t)td.x * args.as_row;
       for (int kb = 0; kb < nkb; ++kb) {
-        const int s = it % NSTAGE;
-        const uint32_t ph = (it / NSTAGE) & 1;
-        const int j = it % C::NSLOT;
-        const uint32_t jph = (it / C::NSLOT) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1, s_abort) || !mbar_wait(&sfree[j], jph ^ 1, s_abort)) {
+        if (!mbar_wait(&empty[st.i], st.ph ^ 1, s_abort) || !mbar_wait(&sfree[sl.i], sl.ph ^ 1, s_abort)) {
           alive = false;
           break;
         }
         if (lane == 0) {
-          uint8_t* st = smem + s * C::STAGE_BYTES;
-          mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+          uint8_t* sp = smem + st.i * C::STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[st.i], C::STAGE_BYTES);
 #pragma unroll
-          for (int a = 0; a < NACC; ++a) tma_load_2d(st + a * C::A_BYTES, &args.tmA[set][a], &full[s], kb * 128, arow);
-          tma_load_2d(st + NACC * C::A_BYTES, &args.tmB, &full[s], kb * 128, td.x);
+          for (int a = 0; a < NACC; ++a) tma_load_2d(sp + a * C::A_BYTES, &args.tmA[set][a], &full[st.i], kb * 128, arow);
+          tma_load_2d(sp + NACC * C::A_BYTES, &args.tmB, &full[st.i], kb * 128, td.x);
         }
-        float* slot = slots + j * C::SLOT_FLOATS;
+        float* slot = raw + sl.i * C::RAW_FLOATS;
 #pragma unroll
         for (int u = 0; u < BN / 32; ++u) {
           const int r = lane + 32 * u;
-          if (r < nr) cp_async_4(slot + r, args.as + (int64_t)(td.x + r) * args.as_row + (int64_t)kb * args.as_kb);
+          if (r < nr) cp_async_4(slot + r, asp + (int64_t)r * args.as_row + (int64_t)kb * args.as_kb);
         }
         if (lane < NACC) cp_async_4(slot + BN + lane, wsp + kb);
-        cp_async_mbar_arrive(&sready[j]);
-        ++it;
+        cp_async_mbar_arrive(&sready[sl.i]);
+        st.next();
+        sl.next();
+        ++issued;
       }
     }
     cp_async_wait_all();
     // no copy into this CTA's shared memory may outlive the CTA
     if (lane == 0) {
-      const uint32_t first = it > (uint32_t)NSTAGE ? it - NSTAGE : 0;
-      for (uint32_t q = first; q < it; ++q) wait_plain(&full[q % NSTAGE], (q / NSTAGE) & 1, kWaitTimeoutNs);
+      const uint32_t first = issued > (uint32_t)NSTAGE ? issued - NSTAGE : 0;
+      for (uint32_t q = first; q < issued; ++q) wait_plain(&full[q % NSTAGE], (q / NSTAGE) & 1, kWaitTimeoutNs);
     }
     __syncwarp();
-  } else if (warp >= 1 && warp <= C::NISSUE) {
-    // ───────────── MMA issuers: warp 1+i takes K-block steps it % NISSUE == i ─────────────
-    // A single thread sustains about one tcgen05.mma per 67 cycles, so two issuers keep the
-    // tensor core fed at small N.  Every K-block step has its own stage and TMEM buffer, so the
-    // issuers never touch the same accumulator and results do not depend on their interleaving.
+  } else if (warp == 1 || warp == 2) {
+    // ───────────── MMA issuers: warp 1 takes even K steps, warp 2 odd ones ─────────────
     const int me = warp - 1;
-    uint32_t it = 0, ait = 0;
+    Ring<NSTAGE> st;
+    Ring<NBUF> bf;
+    uint32_t step = 0;
     bool alive = true;
     for (int tile = blockIdx.x; tile < ntiles && alive; tile += gridDim.x) {
-      const int4 td = args.tiles[tile];
-      const int set = td.z >> 24, e = td.z & 0xFFFFFF;
-      const int nr = td.y;
+      const int nr = args.tiles[tile].y;
       int n_eff = (nr + 15) & ~15;
       n_eff = n_eff < 16 ? 16 : (n_eff > BN ? BN : n_eff);
       const uint32_t idesc = umma_idesc_e4m3(128, n_eff);
-      for (int kb = 0; kb < nkb; ++kb) {
-        if ((int)(it % C::NISSUE) != me) {
-          ++it;
-          ++ait;
-          continue;
-        }
-        const int b = ait % NBUF;
-        const uint32_t aph = (ait / NBUF) & 1;
-        if (!mbar_wait(&acce[b], aph ^ 1, s_abort)) {
-          alive = false;
-          break;
-        }
-        const int s = it % NSTAGE;
-        const uint32_t ph = (it / NSTAGE) & 1;
-        if (!mbar_wait(&full[s], ph, s_abort)) {
+      for (int kb = 0; kb < nkb; ++kb, ++step, st.next(), bf.next()) {
+        if ((int)(step & 1) != me) continue;
+        if (!mbar_wait(&acce[bf.i], bf.ph ^ 1, s_abort) || !mbar_wait(&full[st.i], st.ph, s_abort)) {
           alive = false;
           break;
         }
         tc_fence_after();
         if (lane == 0) {
-          uint8_t* st = smem + s * C::STAGE_BYTES;
-          const uint64_t bdesc = umma_desc_sw128(smem_u32(st + NACC * C::A_BYTES));
+          uint8_t* sp = smem + st.i * C::STAGE_BYTES;
+          const uint64_t bdesc = umma_desc_sw128(smem_u32(sp + NACC * C::A_BYTES));
           uint64_t adesc[NACC];
 #pragma unroll
-          for (int a = 0; a < NACC; ++a) adesc[a] = umma_desc_sw128(smem_u32(st + a * C::A_BYTES));
-          const uint32_t d0 = tmem + (uint32_t)(b * NACC * BN);
+          for (int a = 0; a < NACC; ++a) adesc[a] = umma_desc_sw128(smem_u32(sp + a * C::A_BYTES));
+          const uint32_t d0 = tmem + (uint32_t)(bf.i * NACC * BN);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
 #pragma unroll
             for (int a = 0; a < NACC; ++a)
               umma_f8(d0 + (uint32_t)(a * BN), adesc[a] + 2 * kk, bdesc + 2 * kk, idesc, kk > 0 ? 1u : 0u);
           }
-          umma_commit(&empty[s]);
-          umma_commit(&accf[b]);
+          umma_commit(&empty[st.i]);
+          umma_commit(&accf[bf.i]);
         }
         __syncwarp();
-        ++it;
-        ++ait;
       }
     }
     // every MMA must have completed before TMEM is released
@@ -250,12 +264,40 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
       wait_plain(&drain[me], 0, kWaitTimeoutNs);
     }
     __syncwarp();
-  } else if (warp >= 4) {
+  } else if (warp == 3) {
+    // ───────────── scale warp: combined scale per column and accumulator, once per K step ─────────────
+    Ring<NSLOT> sl;
+    bool alive = true;
+    for (int tile = blockIdx.x; tile < ntiles && alive; tile += gridDim.x) {
+      const int nr = args.tiles[tile].y;
+      for (int kb = 0; kb < nkb; ++kb, sl.next()) {
+        if (!mbar_wait(&sready[sl.i], sl.ph, s_abort)) {
+          alive = false;
+          break;
+        }
+        const float* slot = raw + sl.i * C::RAW_FLOATS;
+        float* sc = scl + sl.i * C::SCL_FLOATS;
+#pragma unroll
+        for (int a = 0; a < NACC; ++a) {
+          const float w = slot[BN + a];
+#pragma unroll
+          for (int u = 0; u < BN / 32; ++u) {
+            const int r = lane + 32 * u;
+            sc[a * BN + r] = r < nr ? slot[r] * w : 0.f;
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&cready[sl.i]);
+      }
+    }
+  } else {
     // ───────────── epilogue warpgroups ─────────────
     const int ew = warp - 4, wg = ew >> 2, q = warp & 3;
     const int lrow = q * 32 + lane;
     const uint32_t tlane = (uint32_t)(q * 32) << 16;
-    uint32_t ait = 0, ephase = 0;
+    Ring<NBUF> bf;
+    Ring<NSLOT> sl;
+    uint32_t ephase = 0;
     bool alive = true;
     // the 4 warps of this warpgroup meet (bounded) before and after sharing the amax slots
     auto wg_sync = [&]() -> bool {
@@ -270,73 +312,55 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
       const int nr = td.y;
       int n_eff = (nr + 15) & ~15;
       n_eff = n_eff < 16 ? 16 : (n_eff > BN ? BN : n_eff);
+      // 32-column groups of this warpgroup's slice that hold real columns
+      const int span = n_eff - wg * CW;
+      const int ngroups = span <= 0 ? 0 : (span >= CW ? CW / 32 : (span + 31) / 32);
       float acc[NACC][CW];
 #pragma unroll
       for (int a = 0; a < NACC; ++a)
 #pragma unroll
         for (int c = 0; c < CW; ++c) acc[a][c] = 0.f;
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int b = ait % NBUF;
-        const uint32_t aph = (ait / NBUF) & 1;
-        if (!mbar_wait(&accf[b], aph, s_abort)) {
+      for (int kb = 0; kb < nkb; ++kb, bf.next(), sl.next()) {
+        if (!mbar_wait(&accf[bf.i], bf.ph, s_abort) || !mbar_wait(&cready[sl.i], sl.ph, s_abort)) {
           alive = false;
           break;
         }
         tc_fence_after();
-        // this K block's scales: a_scale per column (token row) and w_scale per accumulator
-        const int j = ait % C::NSLOT;
-        if (!mbar_wait(&sready[j], (ait / C::NSLOT) & 1, s_abort)) {
-          alive = false;
-          break;
-        }
-        const float* slot = slots + j * C::SLOT_FLOATS;
-        // 32 columns per TMEM load; the buffer is handed back to the MMA warps as soon as the
-        // last load of this K block has landed
-        // 32-column groups of this warpgroup's slice that hold real columns
-        const int span = n_eff - wg * CW;
-        const int ngroups = span <= 0 ? 0 : (span >= CW ? CW / 32 : (span + 31) / 32);
+        const float* sc = scl + sl.i * C::SCL_FLOATS;
         if (ngroups == 0) {
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&acce[b]);
+          if (lane == 0) mbar_arrive(&acce[bf.i]);
         }
 #pragma unroll
         for (int a = 0; a < NACC; ++a) {
 #pragma unroll
           for (int g = 0; g < CW / 32; ++g) {
             const int col = wg * CW + g * 32;
-            const bool last = (a == NACC - 1) && (g == ngroups - 1);
             if (g < ngroups) {
               float pv[32];
-              const uint32_t ta = tmem + tlane + (uint32_t)((b * NACC + a) * BN + col);
+              const uint32_t ta = tmem + tlane + (uint32_t)((bf.i * NACC + a) * BN + col);
               if (col + 32 <= n_eff) tmem_ld32(ta, pv);
               else tmem_ld16p(ta, pv);
               tmem_ld_wait();
-              if (last) {
+              if (a == NACC - 1 && g == ngroups - 1) {  // last load of this step: buffer back to the MMA warps
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&acce[b]);
+                if (lane == 0) mbar_arrive(&acce[bf.i]);
               }
-              const float wsa = slot[BN + a];
-              const float4* sc4 = reinterpret_cast<const float4*>(slot + col);
+              const float4* s4p = reinterpret_cast<const float4*>(sc + a * BN + col);
 #pragma unroll
               for (int i4 = 0; i4 < 8; ++i4) {
-                float4 s4 = sc4[i4];
-                s4.x *= wsa;
-                s4.y *= wsa;
-                s4.z *= wsa;
-                s4.w *= wsa;
-                acc[a][g * 32 + i4 * 4 + 0] = fmaf(pv[i4 * 4 + 0], s4.x, acc[a][g * 32 + i4 * 4 + 0]);
-                acc[a][g * 32 + i4 * 4 + 1] = fmaf(pv[i4 * 4 + 1], s4.y, acc[a][g * 32 + i4 * 4 + 1]);
-                acc[a][g * 32 + i4 * 4 + 2] = fmaf(pv[i4 * 4 + 2], s4.z, acc[a][g * 32 + i4 * 4 + 2]);
-                acc[a][g * 32 + i4 * 4 + 3] = fmaf(pv[i4 * 4 + 3], s4.w, acc[a][g * 32 + i4 * 4 + 3]);
+                const float4 s4 = s4p[i4];
+                float* ac = &acc[a][g * 32 + i4 * 4];
+                fma2(ac[0], ac[1], pv[i4 * 4 + 0], pv[i4 * 4 + 1], s4.x, s4.y);
+                fma2(ac[2], ac[3], pv[i4 * 4 + 2], pv[i4 * 4 + 3], s4.z, s4.w);
               }
             }
           }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sfree[j]);
-        ++ait;
+        if (lane == 0) mbar_arrive(&sfree[sl.i]);
       }
       if (!alive) break;
       const int64_t row0 = td.x;
@@ -358,8 +382,8 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
           if (wg * CW + c >= nr) break;  // warp-uniform
           const float g = bf16_round(acc[0][c]);
           const float u = bf16_round(acc[NACC - 1][c]);
-          const float sl = bf16_round(__fdiv_rn(g, 1.0f + expf(-g)));
-          const float av = bf16_round(sl * u);
+          const float sg = bf16_round(__fdiv_rn(g, 1.0f + expf(-g)));
+          const float av = bf16_round(sg * u);
           acc[0][c] = av;
           const uint32_t m = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(av)));
           if (lane == 0) red[(wg * 4 + q) * CW + c] = __uint_as_float(m);
