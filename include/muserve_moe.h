@@ -4,7 +4,8 @@
  * Every entry point takes raw device pointers, explicit sizes and a CUDA stream, never
  * allocates device memory, never synchronises the stream, and returns an int status
  * (MSV_OK == 0, negative on error; msv_last_error() gives the message).  Work is enqueued
- * on `stream` only, so a caller can capture the calls in a CUDA graph.
+ * on `stream` only, so a caller can capture the calls in a CUDA graph (a statement this
+ * header does not extend to msv_ragged_moe_gemm_fp8_noalloc).
  *
  * Paths cited as `file:line` are in the reference project (xuguanghan/muserve); each entry
  * point names the reference interface it replaces.
@@ -99,6 +100,30 @@ size_t msv_ragged_gemm_workspace_size(int M, int N);
 int msv_ragged_moe_gemm_fp8(const uint8_t* a, const float* a_scale, int M, int K, const uint8_t* w,
                             const float* w_scale, int E, int N, const int32_t* m_indices, void* out,
                             void* workspace, size_t workspace_bytes, msv_stream_t stream);
+
+/*
+ * Allocation-free form of msv_ragged_moe_gemm_fp8: same arguments minus the workspace, same
+ * kernels, same results.  It has no counterpart in the reference.
+ *   Who needs it: callers that cannot hand the library device memory.  A serving engine that
+ *   has given all free HBM to its KV-cache pool has none left for a per-call workspace; a host
+ *   program that binds the reference's signature (which takes no workspace) over an FFI has
+ *   no allocator it can call from that binding; a caller on a latency-critical decode loop
+ *   cannot take the device-wide synchronisation that cudaFree implies.  This entry point
+ *   calls no cudaMalloc, cudaFree or other allocating routine, on the device or (on success)
+ *   the host.
+ *   Scratch: a 4 MiB file-scope device array inside the library, one per device, holding the
+ *   tile list.  Limit: M * (N/128) <= 262128 (e.g. M <= 8191 rows at N = 4096, M <= 32766 at
+ *   N = 1024); larger sizes return MSV_ERR_INVALID with a message naming the limit.
+ *   Set-up: the first call on a device, with that device current, looks up the array's device
+ *   address (cudaGetSymbolAddress) and keeps it; make that first call before any stream
+ *   capture on the device.
+ *   Sharing: every call on one device uses the same array, which keeps the last call's tile
+ *   list.  Calls that run in stream order are safe; calls that overlap on the GPU (different
+ *   streams without ordering between them, or several host threads) race on the array.
+ */
+int msv_ragged_moe_gemm_fp8_noalloc(const uint8_t* a, const float* a_scale, int M, int K, const uint8_t* w,
+                                    const float* w_scale, int E, int N, const int32_t* m_indices, void* out,
+                                    msv_stream_t stream);
 
 /*
  * Dense block-scaled FP8 GEMM, NT:  out[m,n] = bf16(sum_kb (a[m,kb].b[n,kb]) a_s[m,kb] b_s[n/128,kb]).

@@ -48,6 +48,7 @@ _SIGS = {
     "msv_fp8_quant_128": (I, [P, I64, I, I, P, P, I64, P, I64, I64, P]),
     "msv_ragged_gemm_workspace_size": (SZ, [I, I]),
     "msv_ragged_moe_gemm_fp8": (I, [P, P, I, I, P, P, I, I, P, P, P, SZ, P]),
+    "msv_ragged_moe_gemm_fp8_noalloc": (I, [P, P, I, I, P, P, I, I, P, P, P]),
     "msv_gemm_fp8_workspace_size": (SZ, [I, I]),
     "msv_gemm_fp8_nt_groupwise": (I, [P, P, I, I, P, P, I, P, P, SZ, P]),
     "msv_moe_forward_workspace_size": (SZ, [ctypes.POINTER(MoeShape)]),

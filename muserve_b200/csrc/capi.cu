@@ -191,6 +191,59 @@ bool is_pow2_aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr
 }  // namespace
 }  // namespace msv
 
+// ── static scratch of msv_ragged_moe_gemm_fp8_noalloc ────────────────────────────────────
+// The allocation-free ragged GEMM keeps its tile list here instead of in a caller workspace.
+// Layout: the int tile count at byte 0, the int4 tile list from byte 256.  Each device's
+// context holds its own copy; on one device every call shares it.
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;  // 4 MiB
+constexpr size_t kNoAllocTileOffset = 256;
+constexpr size_t kNoAllocMaxTiles = (kNoAllocScratchBytes - kNoAllocTileOffset) / sizeof(int4);  // 262128
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace msv {
+namespace {
+
+uint8_t* g_noalloc_ptr[64];  // device address of g_noalloc_scratch per device, guarded by g_mu
+
+// Set-up, once per device, with that device current: look up the array's device address.
+int noalloc_scratch(uint8_t** out) {
+  int dev = 0;
+  if (int rc = cuda_check(cudaGetDevice(&dev), "cudaGetDevice")) return rc;
+  if (dev < 0 || dev >= 64) return fail(MSV_ERR_UNSUPPORTED, "device index %d", dev);
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    if (int rc = cuda_check(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(g_noalloc_scratch)"))
+      return rc;
+    g_noalloc_ptr[dev] = static_cast<uint8_t*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return MSV_OK;
+}
+
+// Same map as tensor_map() but encoded on every call, outside the host-side cache, so that
+// the allocation-free entry point does not grow a host container either.
+int tensor_map_uncached(CUtensorMap* out, const void* base, uint64_t rows, uint64_t cols, uint64_t stride,
+                        uint32_t box_rows) {
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return fail(MSV_ERR_INVALID, "operand not 16-byte aligned");
+  if (stride % 16 != 0 || cols % 128 != 0) return fail(MSV_ERR_INVALID, "operand row stride / width not multiple of 16/128");
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(MSV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {stride};
+  cuuint32_t box[2] = {128, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MSV_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d) rows=%llu cols=%llu", (int)r,
+                                     (unsigned long long)rows, (unsigned long long)cols);
+  return MSV_OK;
+}
+
+}  // namespace
+}  // namespace msv
+
 using namespace msv;
 
 // ═════════════════════════════════════════════════════════════════════════════════════════
@@ -320,6 +373,56 @@ int msv_ragged_moe_gemm_fp8(const uint8_t* a, const float* a_scale, int M, int K
   if (int rc = tensor_map(&g.tmA[0][0], w, (uint64_t)E * N, K, K, 128)) return rc;
   g.tmA[1][0] = g.tmA[0][0];
   if (int rc = tensor_map(&g.tmB, a, M, K, K, bn)) return rc;
+  g.a_expert_rows[0] = g.a_expert_rows[1] = N;
+  g.ws[0][0] = g.ws[1][0] = w_scale;
+  g.ws[0][1] = g.ws[1][1] = w_scale;
+  g.ws_expert_stride[0] = g.ws_expert_stride[1] = (int64_t)(N / 128) * (K / 128);
+  g.ws_nb_stride = K / 128;
+  g.as = a_scale;
+  g.as_row = K / 128;
+  g.as_kb = 1;
+  g.tiles = tiles;
+  g.num_tiles = ntiles;
+  g.num_kb = K / 128;
+  g.out = out;
+  g.out_ld = N;
+  g.err = d->err_word;
+  return launch_gemm_variant(0, small, g, stream, d->num_sms);
+}
+
+// The kernels and results are those of msv_ragged_moe_gemm_fp8; only the tile list moves from
+// the caller's workspace to g_noalloc_scratch.  Nothing in the scratch has to start at zero:
+// k_tiles_from_runs writes the tile count and every tile below it before the GEMM reads them,
+// so stale contents from an earlier call are never read.  The capacity check uses M * N/128
+// tiles, an upper bound of what k_tiles_from_runs emits (each run of r rows gives at most r
+// row chunks per n-block), so the builder never truncates the list.
+int msv_ragged_moe_gemm_fp8_noalloc(const uint8_t* a, const float* a_scale, int M, int K, const uint8_t* w,
+                                    const float* w_scale, int E, int N, const int32_t* m_indices, void* out,
+                                    msv_stream_t stream) {
+  if (!a || !a_scale || !w || !w_scale || !m_indices || !out || M < 0 || K <= 0 || N <= 0 || E <= 0 ||
+      K % 128 != 0 || N % 128 != 0)
+    return fail(MSV_ERR_INVALID, "msv_ragged_moe_gemm_fp8_noalloc: bad arguments (M=%d K=%d N=%d E=%d)", M, K, N, E);
+  const long long need = (long long)M * (N / 128);
+  if (need > (long long)kNoAllocMaxTiles)
+    return fail(MSV_ERR_INVALID,
+                "msv_ragged_moe_gemm_fp8_noalloc: M * N/128 = %lld tiles exceeds the static scratch limit of %lld "
+                "tiles (%zu bytes); use msv_ragged_moe_gemm_fp8 with a workspace",
+                need, (long long)kNoAllocMaxTiles, kNoAllocScratchBytes);
+  uint8_t* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  DeviceInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  if (M == 0) return MSV_OK;
+  const bool small = (M / E) <= 24;
+  const int bn = variant_bn(0, small), nb = N / 128;
+  int* ntiles = reinterpret_cast<int*>(scratch);
+  int4* tiles = reinterpret_cast<int4*>(scratch + kNoAllocTileOffset);
+  k_tiles_from_runs<<<1, 1024, 0, stream>>>(m_indices, M, bn, nb, tiles, ntiles, (int)need);
+  if (int rc = cuda_check(cudaGetLastError(), "launch tiles_from_runs")) return rc;
+  GemmArgs g{};
+  if (int rc = tensor_map_uncached(&g.tmA[0][0], w, (uint64_t)E * N, K, K, 128)) return rc;
+  g.tmA[1][0] = g.tmA[0][0];
+  if (int rc = tensor_map_uncached(&g.tmB, a, M, K, K, bn)) return rc;
   g.a_expert_rows[0] = g.a_expert_rows[1] = N;
   g.ws[0][0] = g.ws[1][0] = w_scale;
   g.ws[0][1] = g.ws[1][1] = w_scale;
