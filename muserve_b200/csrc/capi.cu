@@ -10,6 +10,7 @@
 
 #include "common.cuh"
 #include "grouped_gemm.cuh"
+#include "grouped_gemm_rows.cuh"
 #include "quant_combine.cuh"
 #include "route.cuh"
 
@@ -88,16 +89,18 @@ EncodeTiledFn encode_fn() {
 struct MapKey {
   uintptr_t base;
   uint64_t rows, cols, stride;
-  uint32_t box_rows;
+  uint32_t box_rows, box_cols, f32;
   bool operator==(const MapKey& o) const {
-    return base == o.base && rows == o.rows && cols == o.cols && stride == o.stride && box_rows == o.box_rows;
+    return base == o.base && rows == o.rows && cols == o.cols && stride == o.stride && box_rows == o.box_rows &&
+           box_cols == o.box_cols && f32 == o.f32;
   }
 };
 struct MapKeyHash {
   size_t operator()(const MapKey& k) const {
     size_t h = k.base * 0x9E3779B97F4A7C15ull;
     h ^= (k.rows + 0x632BE59BD9B4E019ull) + (h << 6) + (h >> 2);
-    h ^= (k.cols * 31 + k.stride * 131 + k.box_rows) + (h << 6) + (h >> 2);
+    h ^= (k.cols * 31 + k.stride * 131 + k.box_rows + ((uint64_t)k.box_cols << 20) + ((uint64_t)k.f32 << 40)) + (h << 6) +
+         (h >> 2);
     return h;
   }
 };
@@ -108,7 +111,7 @@ std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
 int tensor_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t cols, uint64_t stride, uint32_t box_rows) {
   if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return fail(MSV_ERR_INVALID, "operand not 16-byte aligned");
   if (stride % 16 != 0 || cols % 128 != 0) return fail(MSV_ERR_INVALID, "operand row stride / width not multiple of 16/128");
-  MapKey key{reinterpret_cast<uintptr_t>(base), rows, cols, stride, box_rows};
+  MapKey key{reinterpret_cast<uintptr_t>(base), rows, cols, stride, box_rows, 128, 0};
   {
     std::lock_guard<std::mutex> lk(g_mu);
     auto it = g_maps.find(key);
@@ -136,12 +139,47 @@ int tensor_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t cols,
   return MSV_OK;
 }
 
+// 2-D fp32 matrix [rows, cols] with row stride `stride` bytes (a multiple of 16), box
+// [box_rows x box_cols] (box_cols * 4 a multiple of 16), no swizzle, zero fill out of bounds.
+int tensor_map_f32(CUtensorMap* out, const void* base, uint64_t rows, uint64_t cols, uint64_t stride, uint32_t box_cols,
+                   uint32_t box_rows) {
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0 || stride % 16 != 0 || (box_cols * 4) % 16 != 0)
+    return fail(MSV_ERR_INVALID, "fp32 scale matrix not 16-byte aligned (base, row stride or box width)");
+  MapKey key{reinterpret_cast<uintptr_t>(base), rows, cols, stride, box_rows, box_cols, 1};
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_maps.find(key);
+    if (it != g_maps.end()) {
+      *out = it->second;
+      return MSV_OK;
+    }
+  }
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(MSV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {stride};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MSV_ERR_INVALID, "cuTensorMapEncodeTiled (fp32) failed (%d) rows=%llu cols=%llu", (int)r,
+                                     (unsigned long long)rows, (unsigned long long)cols);
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_maps.size() > 8192) g_maps.clear();
+  g_maps.emplace(key, m);
+  *out = m;
+  return MSV_OK;
+}
+
 // ── grouped GEMM variants ────────────────────────────────────────────────────────────────
 
 using G1Small = GemmCfg<32, 2, 1, 1>;   // gate+up -> SwiGLU -> e4m3, <= 32 rows per chunk
-using G1Large = GemmCfg<96, 2, 1, 3>;   // same, <= 96 rows per chunk (3 epilogue warpgroups)
 using G2Small = GemmCfg<32, 1, 0, 1>;   // plain -> bf16, <= 32 rows per chunk
 using G2Large = GemmCfg<192, 1, 0, 3>;  // plain -> bf16, <= 192 rows per chunk
+using R1 = RowsCfg<1>;                  // tokens on M: gate+up halves -> SwiGLU -> e4m3
+using R2 = RowsCfg<0>;                  // tokens on M: plain -> bf16
 
 template <class C>
 int launch_gemm(const GemmArgs& a, cudaStream_t st, int num_sms) {
@@ -159,14 +197,26 @@ int launch_gemm(const GemmArgs& a, cudaStream_t st, int num_sms) {
   return cuda_check(cudaGetLastError(), "launch grouped_gemm");
 }
 
-int launch_gemm_variant(int epi, bool small, const GemmArgs& a, cudaStream_t st, int nsm) {
-  if (epi == 1) return small ? launch_gemm<G1Small>(a, st, nsm) : launch_gemm<G1Large>(a, st, nsm);
+template <class C>
+int launch_gemm_rows(const RowsArgs& a, cudaStream_t st, int num_sms) {
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!configured[dev]) {
+    if (int rc = cuda_check(cudaFuncSetAttribute(k_grouped_gemm_rows<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 C::SMEM_BYTES),
+                            "cudaFuncSetAttribute(grouped_gemm_rows)"))
+      return rc;
+    configured[dev] = true;
+  }
+  k_grouped_gemm_rows<C><<<num_sms, C::THREADS, C::SMEM_BYTES, st>>>(a);
+  return cuda_check(cudaGetLastError(), "launch grouped_gemm_rows");
+}
+
+int launch_gemm_variant(bool small, const GemmArgs& a, cudaStream_t st, int nsm) {
   return small ? launch_gemm<G2Small>(a, st, nsm) : launch_gemm<G2Large>(a, st, nsm);
 }
-int variant_bn(int epi, bool small) {
-  if (epi == 1) return small ? G1Small::BN : G1Large::BN;
-  return small ? G2Small::BN : G2Large::BN;
-}
+int variant_bn(bool small) { return small ? G2Small::BN : G2Large::BN; }
 
 // ── workspace carving ────────────────────────────────────────────────────────────────────
 
@@ -362,7 +412,7 @@ int msv_ragged_moe_gemm_fp8(const uint8_t* a, const float* a_scale, int M, int K
   DeviceInfo* d = nullptr;
   if (int rc = device_info(&d)) return rc;
   const bool small = (M / E) <= 24;
-  const int bn = variant_bn(0, small), nb = N / 128;
+  const int bn = variant_bn(small), nb = N / 128;
   const size_t cap = tile_cap(M, M, 32, nb);
   Carver c{static_cast<uint8_t*>(workspace)};
   int4* tiles = c.take<int4>(cap);
@@ -387,7 +437,7 @@ int msv_ragged_moe_gemm_fp8(const uint8_t* a, const float* a_scale, int M, int K
   g.out = out;
   g.out_ld = N;
   g.err = d->err_word;
-  return launch_gemm_variant(0, small, g, stream, d->num_sms);
+  return launch_gemm_variant(small, g, stream, d->num_sms);
 }
 
 // The kernels and results are those of msv_ragged_moe_gemm_fp8; only the tile list moves from
@@ -414,7 +464,7 @@ int msv_ragged_moe_gemm_fp8_noalloc(const uint8_t* a, const float* a_scale, int 
   if (int rc = device_info(&d)) return rc;
   if (M == 0) return MSV_OK;
   const bool small = (M / E) <= 24;
-  const int bn = variant_bn(0, small), nb = N / 128;
+  const int bn = variant_bn(small), nb = N / 128;
   int* ntiles = reinterpret_cast<int*>(scratch);
   int4* tiles = reinterpret_cast<int4*>(scratch + kNoAllocTileOffset);
   k_tiles_from_runs<<<1, 1024, 0, stream>>>(m_indices, M, bn, nb, tiles, ntiles, (int)need);
@@ -437,7 +487,7 @@ int msv_ragged_moe_gemm_fp8_noalloc(const uint8_t* a, const float* a_scale, int 
   g.out = out;
   g.out_ld = N;
   g.err = d->err_word;
-  return launch_gemm_variant(0, small, g, stream, d->num_sms);
+  return launch_gemm_variant(small, g, stream, d->num_sms);
 }
 
 size_t msv_gemm_fp8_workspace_size(int M, int N) {
@@ -458,7 +508,7 @@ int msv_gemm_fp8_nt_groupwise(const uint8_t* a, const float* a_scale, int M, int
   DeviceInfo* d = nullptr;
   if (int rc = device_info(&d)) return rc;
   const bool small = M <= 32;
-  const int bn = variant_bn(0, small), nb = N / 128;
+  const int bn = variant_bn(small), nb = N / 128;
   Carver c{static_cast<uint8_t*>(workspace)};
   int4* tiles = c.take<int4>(tile_cap(1, M, 32, nb));
   int* ntiles = c.take<int>(1);
@@ -481,7 +531,7 @@ int msv_gemm_fp8_nt_groupwise(const uint8_t* a, const float* a_scale, int M, int
   g.out = out;
   g.out_ld = N;
   g.err = d->err_word;
-  return launch_gemm_variant(0, small, g, stream, d->num_sms);
+  return launch_gemm_variant(small, g, stream, d->num_sms);
 }
 
 // ── whole layer ──────────────────────────────────────────────────────────────────────────
@@ -489,8 +539,8 @@ int msv_gemm_fp8_nt_groupwise(const uint8_t* a, const float* a_scale, int M, int
 namespace {
 struct LayerPlan {
   int T, H, E, k, I, Is, P, rows, e_local;
-  bool shared, small1, small2;
-  int bn1, bn2, nb1, nb2;
+  bool shared, small1, small2, rows1, rows2;
+  int bn1, bn2, nb1, nb2, srows;
   size_t cap1, cap2;
 };
 
@@ -518,10 +568,16 @@ int plan_layer(const msv_moe_shape* s, LayerPlan* L) {
   const double avg = (double)L->P / (s->placement ? (double)s->tp : 1.0) / (double)L->e_local;
   L->small1 = avg <= 24.0;
   L->small2 = avg <= 24.0;
-  L->bn1 = variant_bn(1, L->small1);
-  L->bn2 = variant_bn(0, L->small2);
+  // large batches: tokens on the MMA's M side (128-row token chunks).  That kernel loads the
+  // tile's K blocks in pairs and its scales as one box, so it needs K/128 a multiple of 4 and
+  // at most 32; other large shapes use the weight-rows kernels.
+  L->rows1 = !L->small1 && (L->H / 128) % 4 == 0 && L->H / 128 <= R1::MAXKB;
+  L->rows2 = !L->small2 && (L->I / 128) % 4 == 0 && L->I / 128 <= R2::MAXKB;
+  L->bn1 = L->rows1 ? R1::BM : G1Small::BN;
+  L->bn2 = L->rows2 ? R2::BM : (L->small2 ? G2Small::BN : G2Large::BN);
   L->nb1 = L->I / 128;
   L->nb2 = L->H / 128;
+  L->srows = (L->rows + 3) & ~3;  // K-block stride of the activation scales (16-byte rows)
   L->cap1 = tile_cap(L->e_local, L->P, L->bn1, L->nb1) + (size_t)L->nb1 * ((L->T + L->bn1 - 1) / L->bn1 + 1);
   L->cap2 = tile_cap(L->e_local, L->P, L->bn2, L->nb2) + (size_t)L->nb2 * ((L->T + L->bn2 - 1) / L->bn2 + 1);
   return MSV_OK;
@@ -550,9 +606,9 @@ size_t carve_layer(const LayerPlan& L, uint8_t* base, LayerWs* w) {
   w->tiles2 = c.take<int4>(L.cap2);
   w->ntiles2 = c.take<int>(1);
   w->xq = c.take<uint8_t>((size_t)L.rows * L.H);
-  w->xs = c.take<float>((size_t)L.rows * (L.H / 128));
+  w->xs = c.take<float>((size_t)L.srows * (L.H / 128));
   w->aq = c.take<uint8_t>((size_t)L.rows * L.I);
-  w->as = c.take<float>((size_t)L.rows * (L.I / 128));
+  w->as = c.take<float>((size_t)L.srows * (L.I / 128));
   w->down = c.take<__nv_bfloat16>((size_t)L.rows * L.H);
   w->gate_val = c.take<float>((size_t)(L.T > 0 ? L.T : 1));
   return c.off + 256;
@@ -655,76 +711,146 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
   q.ldq = L.H;
   q.scale = w.xs;
   q.s_row = 1;
-  q.s_kb = L.rows;
+  q.s_kb = L.srows;
   q.gate_w = (do_shared && W->sh_gate_logit_w) ? static_cast<const __nv_bfloat16*>(W->sh_gate_logit_w) : nullptr;
   q.gate_val = w.gate_val;
   k_quant_rows<<<(L.rows + kQuantWarps - 1) / kQuantWarps, kQuantWarps * 32, 0, stream>>>(q);
   if (int rc = cuda_check(cudaGetLastError(), "launch quant")) return rc;
   if (int rc = mark(3)) return rc;
   // 4. gate_up GEMM with SwiGLU + requant epilogue
-  GemmArgs g1{};
   const uint64_t gu_rows = (uint64_t)(L.e_local - 1) * W->gu_expert_rows + L.I;
-  if (int rc = tensor_map(&g1.tmA[0][0], W->gate_w, gu_rows, L.H, L.H, 128)) return rc;
-  if (int rc = tensor_map(&g1.tmA[0][1], W->up_w, gu_rows, L.H, L.H, 128)) return rc;
-  if (L.shared) {
-    if (int rc = tensor_map(&g1.tmA[1][0], W->sh_gate_w, L.Is, L.H, L.H, 128)) return rc;
-    if (int rc = tensor_map(&g1.tmA[1][1], W->sh_up_w, L.Is, L.H, L.H, 128)) return rc;
+  const int nkb1 = L.H / 128, nkb2 = L.I / 128;
+  if (L.rows1) {
+    RowsArgs r{};
+    if (int rc = tensor_map(&r.tmTok, w.xq, L.rows, L.H, L.H, R1::BM)) return rc;
+    if (int rc = tensor_map(&r.tmW[0][0], W->gate_w, gu_rows, L.H, L.H, 64)) return rc;
+    if (int rc = tensor_map(&r.tmW[0][1], W->up_w, gu_rows, L.H, L.H, 64)) return rc;
+    const int64_t rpe = W->gu_scale_expert_stride / nkb1;  // scale rows between experts
+    const uint64_t gs_rows = (uint64_t)(L.e_local - 1) * rpe + L.I / 128;
+    if (int rc = tensor_map_f32(&r.tmWS[0][0], W->gate_s, gs_rows, nkb1, (uint64_t)nkb1 * 4, nkb1, 1)) return rc;
+    if (int rc = tensor_map_f32(&r.tmWS[0][1], W->up_s, gs_rows, nkb1, (uint64_t)nkb1 * 4, nkb1, 1)) return rc;
+    if (L.shared) {
+      if (int rc = tensor_map(&r.tmW[1][0], W->sh_gate_w, L.Is, L.H, L.H, 64)) return rc;
+      if (int rc = tensor_map(&r.tmW[1][1], W->sh_up_w, L.Is, L.H, L.H, 64)) return rc;
+      if (int rc = tensor_map_f32(&r.tmWS[1][0], W->sh_gate_s, L.Is / 128, nkb1, (uint64_t)nkb1 * 4, nkb1, 1)) return rc;
+      if (int rc = tensor_map_f32(&r.tmWS[1][1], W->sh_up_s, L.Is / 128, nkb1, (uint64_t)nkb1 * 4, nkb1, 1)) return rc;
+    } else {
+      r.tmW[1][0] = r.tmW[0][0];
+      r.tmW[1][1] = r.tmW[0][1];
+      r.tmWS[1][0] = r.tmWS[0][0];
+      r.tmWS[1][1] = r.tmWS[0][1];
+    }
+    if (int rc = tensor_map_f32(&r.tmAS, w.xs, nkb1, L.srows, (uint64_t)L.srows * 4, R1::SC_LD, nkb1)) return rc;
+    r.w_rows[0] = (int)W->gu_expert_rows;
+    r.w_rows[1] = 0;
+    r.ws_rows[0] = (int)rpe;
+    r.ws_rows[1] = 0;
+    r.tiles = w.tiles1;
+    r.num_tiles = w.ntiles1;
+    r.num_kb = nkb1;
+    r.out = w.aq;
+    r.out_ld = L.I;
+    r.out_scale = w.as;
+    r.os_row = 1;
+    r.os_kb = L.srows;
+    r.err = d->err_word;
+    if (int rc = launch_gemm_rows<R1>(r, stream, d->num_sms)) return rc;
   } else {
-    g1.tmA[1][0] = g1.tmA[0][0];
-    g1.tmA[1][1] = g1.tmA[0][1];
+    GemmArgs g1{};
+    if (int rc = tensor_map(&g1.tmA[0][0], W->gate_w, gu_rows, L.H, L.H, 128)) return rc;
+    if (int rc = tensor_map(&g1.tmA[0][1], W->up_w, gu_rows, L.H, L.H, 128)) return rc;
+    if (L.shared) {
+      if (int rc = tensor_map(&g1.tmA[1][0], W->sh_gate_w, L.Is, L.H, L.H, 128)) return rc;
+      if (int rc = tensor_map(&g1.tmA[1][1], W->sh_up_w, L.Is, L.H, L.H, 128)) return rc;
+    } else {
+      g1.tmA[1][0] = g1.tmA[0][0];
+      g1.tmA[1][1] = g1.tmA[0][1];
+    }
+    if (int rc = tensor_map(&g1.tmB, w.xq, L.rows, L.H, L.H, L.bn1)) return rc;
+    g1.a_expert_rows[0] = (int)W->gu_expert_rows;
+    g1.a_expert_rows[1] = 0;
+    g1.ws[0][0] = W->gate_s;
+    g1.ws[0][1] = W->up_s;
+    g1.ws[1][0] = L.shared ? W->sh_gate_s : W->gate_s;
+    g1.ws[1][1] = L.shared ? W->sh_up_s : W->up_s;
+    g1.ws_expert_stride[0] = W->gu_scale_expert_stride;
+    g1.ws_expert_stride[1] = 0;
+    g1.ws_nb_stride = nkb1;
+    g1.as = w.xs;
+    g1.as_row = 1;
+    g1.as_kb = L.srows;
+    g1.tiles = w.tiles1;
+    g1.num_tiles = w.ntiles1;
+    g1.num_kb = nkb1;
+    g1.out = w.aq;
+    g1.out_ld = L.I;
+    g1.out_scale = w.as;
+    g1.os_row = 1;
+    g1.os_kb = L.srows;
+    g1.err = d->err_word;
+    if (int rc = launch_gemm<G1Small>(g1, stream, d->num_sms)) return rc;
   }
-  if (int rc = tensor_map(&g1.tmB, w.xq, L.rows, L.H, L.H, L.bn1)) return rc;
-  g1.a_expert_rows[0] = (int)W->gu_expert_rows;
-  g1.a_expert_rows[1] = 0;
-  g1.ws[0][0] = W->gate_s;
-  g1.ws[0][1] = W->up_s;
-  g1.ws[1][0] = L.shared ? W->sh_gate_s : W->gate_s;
-  g1.ws[1][1] = L.shared ? W->sh_up_s : W->up_s;
-  g1.ws_expert_stride[0] = W->gu_scale_expert_stride;
-  g1.ws_expert_stride[1] = 0;
-  g1.ws_nb_stride = L.H / 128;
-  g1.as = w.xs;
-  g1.as_row = 1;
-  g1.as_kb = L.rows;
-  g1.tiles = w.tiles1;
-  g1.num_tiles = w.ntiles1;
-  g1.num_kb = L.H / 128;
-  g1.out = w.aq;
-  g1.out_ld = L.I;
-  g1.out_scale = w.as;
-  g1.os_row = 1;
-  g1.os_kb = L.rows;
-  g1.err = d->err_word;
-  if (int rc = launch_gemm_variant(1, L.small1, g1, stream, d->num_sms)) return rc;
   if (int rc = mark(4)) return rc;
   // 5. down GEMM
-  GemmArgs g2{};
-  if (int rc = tensor_map(&g2.tmA[0][0], W->down_w, (uint64_t)L.e_local * L.H, L.I, L.I, 128)) return rc;
-  if (L.shared) {
-    if (int rc = tensor_map(&g2.tmA[1][0], W->sh_down_w, L.H, L.Is, L.Is, 128)) return rc;
+  if (L.rows2) {
+    RowsArgs r{};
+    if (int rc = tensor_map(&r.tmTok, w.aq, L.rows, L.I, L.I, R2::BM)) return rc;
+    if (int rc = tensor_map(&r.tmW[0][0], W->down_w, (uint64_t)L.e_local * L.H, L.I, L.I, 128)) return rc;
+    if (int rc = tensor_map_f32(&r.tmWS[0][0], W->down_s, (uint64_t)L.e_local * (L.H / 128), nkb2, (uint64_t)nkb2 * 4,
+                                nkb2, 1))
+      return rc;
+    if (L.shared) {
+      if (int rc = tensor_map(&r.tmW[1][0], W->sh_down_w, L.H, L.Is, L.Is, 128)) return rc;
+      if (int rc = tensor_map_f32(&r.tmWS[1][0], W->sh_down_s, L.H / 128, nkb2, (uint64_t)nkb2 * 4, nkb2, 1)) return rc;
+    } else {
+      r.tmW[1][0] = r.tmW[0][0];
+      r.tmWS[1][0] = r.tmWS[0][0];
+    }
+    r.tmW[0][1] = r.tmW[0][0];
+    r.tmW[1][1] = r.tmW[1][0];
+    r.tmWS[0][1] = r.tmWS[0][0];
+    r.tmWS[1][1] = r.tmWS[1][0];
+    if (int rc = tensor_map_f32(&r.tmAS, w.as, nkb2, L.srows, (uint64_t)L.srows * 4, R2::SC_LD, nkb2)) return rc;
+    r.w_rows[0] = L.H;
+    r.w_rows[1] = 0;
+    r.ws_rows[0] = L.H / 128;
+    r.ws_rows[1] = 0;
+    r.tiles = w.tiles2;
+    r.num_tiles = w.ntiles2;
+    r.num_kb = nkb2;
+    r.out = w.down;
+    r.out_ld = L.H;
+    r.err = d->err_word;
+    if (int rc = launch_gemm_rows<R2>(r, stream, d->num_sms)) return rc;
   } else {
-    g2.tmA[1][0] = g2.tmA[0][0];
+    GemmArgs g2{};
+    if (int rc = tensor_map(&g2.tmA[0][0], W->down_w, (uint64_t)L.e_local * L.H, L.I, L.I, 128)) return rc;
+    if (L.shared) {
+      if (int rc = tensor_map(&g2.tmA[1][0], W->sh_down_w, L.H, L.Is, L.Is, 128)) return rc;
+    } else {
+      g2.tmA[1][0] = g2.tmA[0][0];
+    }
+    g2.tmA[0][1] = g2.tmA[0][0];
+    g2.tmA[1][1] = g2.tmA[1][0];
+    if (int rc = tensor_map(&g2.tmB, w.aq, L.rows, L.I, L.I, L.bn2)) return rc;
+    g2.a_expert_rows[0] = L.H;
+    g2.a_expert_rows[1] = 0;
+    g2.ws[0][0] = g2.ws[0][1] = W->down_s;
+    g2.ws[1][0] = g2.ws[1][1] = L.shared ? W->sh_down_s : W->down_s;
+    g2.ws_expert_stride[0] = (int64_t)(L.H / 128) * nkb2;
+    g2.ws_expert_stride[1] = 0;
+    g2.ws_nb_stride = nkb2;
+    g2.as = w.as;
+    g2.as_row = 1;
+    g2.as_kb = L.srows;
+    g2.tiles = w.tiles2;
+    g2.num_tiles = w.ntiles2;
+    g2.num_kb = nkb2;
+    g2.out = w.down;
+    g2.out_ld = L.H;
+    g2.err = d->err_word;
+    if (int rc = launch_gemm_variant(L.small2, g2, stream, d->num_sms)) return rc;
   }
-  g2.tmA[0][1] = g2.tmA[0][0];
-  g2.tmA[1][1] = g2.tmA[1][0];
-  if (int rc = tensor_map(&g2.tmB, w.aq, L.rows, L.I, L.I, L.bn2)) return rc;
-  g2.a_expert_rows[0] = L.H;
-  g2.a_expert_rows[1] = 0;
-  g2.ws[0][0] = g2.ws[0][1] = W->down_s;
-  g2.ws[1][0] = g2.ws[1][1] = L.shared ? W->sh_down_s : W->down_s;
-  g2.ws_expert_stride[0] = (int64_t)(L.H / 128) * (L.I / 128);
-  g2.ws_expert_stride[1] = 0;
-  g2.ws_nb_stride = L.I / 128;
-  g2.as = w.as;
-  g2.as_row = 1;
-  g2.as_kb = L.rows;
-  g2.tiles = w.tiles2;
-  g2.num_tiles = w.ntiles2;
-  g2.num_kb = L.I / 128;
-  g2.out = w.down;
-  g2.out_ld = L.H;
-  g2.err = d->err_word;
-  if (int rc = launch_gemm_variant(0, L.small2, g2, stream, d->num_sms)) return rc;
   if (int rc = mark(5)) return rc;
   // 6. weighted combine (+ shared expert)
   CombineArgs cb{};

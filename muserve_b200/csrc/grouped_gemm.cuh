@@ -95,7 +95,7 @@ struct GemmCfg {
 
 MSV_DEVICE bool wait_plain(uint64_t* bar, uint32_t parity, unsigned long long limit_ns) {
   unsigned long long t0 = globaltimer();
-  while (!mbar_try_wait(bar, parity))
+  while (!mbar_try_wait_sleep(bar, parity, kSuspendNs))
     if (globaltimer() - t0 > limit_ns) return false;
   return true;
 }
