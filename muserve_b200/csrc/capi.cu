@@ -139,6 +139,40 @@ int tensor_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t cols,
   return MSV_OK;
 }
 
+// 3-D view of an e4m3 (byte) matrix [rows, cols] as [cols/128][rows][128 B]: box [nkb blocks x
+// box_rows x 128 B], 128-byte swizzle, zero fill; one load brings nkb consecutive K blocks.
+int tensor_map_kblocks(CUtensorMap* out, const void* base, uint64_t rows, uint64_t cols, uint64_t stride,
+                       uint32_t box_rows, uint32_t nkb) {
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return fail(MSV_ERR_INVALID, "operand not 16-byte aligned");
+  if (stride % 16 != 0 || cols % 128 != 0) return fail(MSV_ERR_INVALID, "operand row stride / width not multiple of 16/128");
+  MapKey key{reinterpret_cast<uintptr_t>(base), rows, cols, stride, box_rows, nkb, 2};
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_maps.find(key);
+    if (it != g_maps.end()) {
+      *out = it->second;
+      return MSV_OK;
+    }
+  }
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(MSV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  CUtensorMap m;
+  cuuint64_t dims[3] = {128, rows, cols / 128};
+  cuuint64_t strides[2] = {stride, 128};
+  cuuint32_t box[3] = {128, box_rows, nkb};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MSV_ERR_INVALID, "cuTensorMapEncodeTiled (3-D) failed (%d) rows=%llu cols=%llu", (int)r,
+                                     (unsigned long long)rows, (unsigned long long)cols);
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_maps.size() > 8192) g_maps.clear();
+  g_maps.emplace(key, m);
+  *out = m;
+  return MSV_OK;
+}
+
 // 2-D fp32 matrix [rows, cols] with row stride `stride` bytes (a multiple of 16), box
 // [box_rows x box_cols] (box_cols * 4 a multiple of 16), no swizzle, zero fill out of bounds.
 int tensor_map_f32(CUtensorMap* out, const void* base, uint64_t rows, uint64_t cols, uint64_t stride, uint32_t box_cols,
@@ -178,8 +212,8 @@ int tensor_map_f32(CUtensorMap* out, const void* base, uint64_t rows, uint64_t c
 using G1Small = GemmCfg<32, 2, 1, 1>;   // gate+up -> SwiGLU -> e4m3, <= 32 rows per chunk
 using G2Small = GemmCfg<32, 1, 0, 1>;   // plain -> bf16, <= 32 rows per chunk
 using G2Large = GemmCfg<192, 1, 0, 3>;  // plain -> bf16, <= 192 rows per chunk
-using R1 = RowsCfg<1>;                  // tokens on M: gate+up halves -> SwiGLU -> e4m3
-using R2 = RowsCfg<0>;                  // tokens on M: plain -> bf16
+using R1 = RowsCfg<1, 32, 2>;          // tokens on M: gate+up halves -> SwiGLU -> e4m3 (K <= 4096)
+using R2 = RowsCfg<0, 8, 4>;           // tokens on M: plain -> bf16 (K <= 1024)
 
 template <class C>
 int launch_gemm(const GemmArgs& a, cudaStream_t st, int num_sms) {
@@ -722,7 +756,7 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
   const int nkb1 = L.H / 128, nkb2 = L.I / 128;
   if (L.rows1) {
     RowsArgs r{};
-    if (int rc = tensor_map(&r.tmTok, w.xq, L.rows, L.H, L.H, R1::BM)) return rc;
+    if (int rc = tensor_map_kblocks(&r.tmTok, w.xq, L.rows, L.H, L.H, R1::BM, R1::KS)) return rc;
     if (int rc = tensor_map(&r.tmW[0][0], W->gate_w, gu_rows, L.H, L.H, 64)) return rc;
     if (int rc = tensor_map(&r.tmW[0][1], W->up_w, gu_rows, L.H, L.H, 64)) return rc;
     const int64_t rpe = W->gu_scale_expert_stride / nkb1;  // scale rows between experts
@@ -794,13 +828,13 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
   // 5. down GEMM
   if (L.rows2) {
     RowsArgs r{};
-    if (int rc = tensor_map(&r.tmTok, w.aq, L.rows, L.I, L.I, R2::BM)) return rc;
-    if (int rc = tensor_map(&r.tmW[0][0], W->down_w, (uint64_t)L.e_local * L.H, L.I, L.I, 128)) return rc;
+    if (int rc = tensor_map_kblocks(&r.tmTok, w.aq, L.rows, L.I, L.I, R2::BM, R2::KS)) return rc;
+    if (int rc = tensor_map_kblocks(&r.tmW[0][0], W->down_w, (uint64_t)L.e_local * L.H, L.I, L.I, 128, R2::KS)) return rc;
     if (int rc = tensor_map_f32(&r.tmWS[0][0], W->down_s, (uint64_t)L.e_local * (L.H / 128), nkb2, (uint64_t)nkb2 * 4,
                                 nkb2, 1))
       return rc;
     if (L.shared) {
-      if (int rc = tensor_map(&r.tmW[1][0], W->sh_down_w, L.H, L.Is, L.Is, 128)) return rc;
+      if (int rc = tensor_map_kblocks(&r.tmW[1][0], W->sh_down_w, L.H, L.Is, L.Is, 128, R2::KS)) return rc;
       if (int rc = tensor_map_f32(&r.tmWS[1][0], W->sh_down_s, L.H / 128, nkb2, (uint64_t)nkb2 * 4, nkb2, 1)) return rc;
     } else {
       r.tmW[1][0] = r.tmW[0][0];

@@ -148,6 +148,15 @@ MSV_DEVICE void tma_load_2d(void* dst, const CUtensorMap* m, uint64_t* bar, int 
       : "memory");
 }
 
+// 3-D tiled load (no multicast): coordinates {x, y, z}, x a multiple of 16 bytes.
+MSV_DEVICE void tma_load_3d(void* dst, const CUtensorMap* m, uint64_t* bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cta.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
 // ── tcgen05 ─────────────────────────────────────────────────────────────────────────────
 
 // Shared-memory matrix descriptor for a K-major operand tile stored with the 128-byte

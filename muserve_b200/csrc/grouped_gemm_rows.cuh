@@ -20,16 +20,19 @@
 //          each half (its gate and up columns), so SwiGLU needs no exchange, and the per-row
 //          amax for the e4m3 requant is combined across the four warpgroups at tile end.
 //   EPI 0 (plain -> bf16): N = the 128 weight rows of the n-block; warpgroup w owns 32 columns.
-// Roles: warp 0 TMA producer; warp 1 MMA issuer and TMEM owner; warps 2..17 epilogue (warp w
-// reads TMEM lanes 32 * (w % 4) .. +32).  Every wait is bounded.
+// Roles: warp 0 TMA producer of the operand stages; warps 1 and 2 MMA issuers on alternate
+// stages (each owns one TMEM buffer pair, so one issuer's waits overlap the other's MMAs), warp 1
+// also owns TMEM; warp 3 loads the tiles' scales into a ring of NSCB buffers, up to NSCB tiles
+// ahead of the epilogue; warps 4..19 epilogue (warp w reads TMEM lanes 32 * (w % 4) .. +32).
+// Every wait is bounded.
 #pragma once
 #include "grouped_gemm.cuh"
 
 namespace msv {
 
 struct RowsArgs {
-  CUtensorMap tmTok;     // activations [rows, K] e4m3, box 128 rows x 128 B
-  CUtensorMap tmW[2][2]; // weights [set][gate, up] (EPI 1: box 64 rows) or [set][0] (EPI 0: box 128 rows)
+  CUtensorMap tmTok;     // activations as 3-D [K/128][rows][128 B] e4m3, box 2 K blocks x 128 rows
+  CUtensorMap tmW[2][2]; // weights [set][gate, up] (EPI 1: 2-D, box 64 rows) or [set][0] (EPI 0: 3-D like tmTok)
   CUtensorMap tmAS;      // activation scales, fp32 [K/128][srows] (K-block-major), box 132 x K/128
   CUtensorMap tmWS[2][2];// weight scales, fp32 [blocks][K/128], box K/128 x 1
   int w_rows[2];         // weight rows between consecutive experts, per set
@@ -44,35 +47,38 @@ struct RowsArgs {
   int* err;
 };
 
-template <int EPI_>
+template <int EPI_, int MAXKB_, int NSCB_>
 struct RowsCfg {
   static constexpr int EPI = EPI_;
+  static constexpr int MAXKB = MAXKB_;  // K <= 128 * MAXKB
+  static constexpr int NSCB = NSCB_;    // scale buffers (tiles in flight between scale warp and epilogue)
   static constexpr int BM = 128;  // token rows per tile (TMEM lanes)
   static constexpr int BN = 128;  // weight rows per MMA (TMEM columns per buffer)
   static constexpr int KS = 2;    // 128-wide K blocks per pipeline stage
   static constexpr int NHALF = EPI == 1 ? 2 : 1;
   static constexpr int NWG = 4;
-  static constexpr int THREADS = 64 + 128 * NWG;
+  static constexpr int NCTRL = 4;  // producer, two MMA issuers, scale loader
+  static constexpr int THREADS = 32 * NCTRL + 128 * NWG;
   static constexpr int KB_BYTES = 128 * 128;  // one 128 x 128-byte operand tile
   static constexpr int STAGE_BYTES = KS * 2 * KB_BYTES;
   static constexpr int NPAIR = 2;             // TMEM buffer pairs (one pair per stage)
   static constexpr int TMEM_COLS = 512;
-  static constexpr int MAXKB = 32;            // K <= 4096
   static constexpr int SC_LD = BM + 4;        // activation-scale row: the chunk's rows from row0 & ~3
-  static constexpr int SC_FLOATS = SC_LD * MAXKB + 2 * MAXKB;  // + weight scales (gate, up)
+  static constexpr int SC_FLOATS = (SC_LD * MAXKB + 2 * MAXKB + 31) & ~31;  // + weight scales (gate, up); 128-byte multiple
   static constexpr int SC_BYTES = SC_FLOATS * 4;
   static constexpr int SMEM_LIMIT = 232448 - 1024;
-  static constexpr int BAR_BYTES = 16 * 8;
-  static constexpr int NSTAGE_RAW = (SMEM_LIMIT - 2 * SC_BYTES - BAR_BYTES - 16) / STAGE_BYTES;
+  static constexpr int BAR_BYTES = 24 * 8;
+  static constexpr int NSTAGE_RAW = (SMEM_LIMIT - NSCB * SC_BYTES - BAR_BYTES - 16) / STAGE_BYTES;
   static constexpr int NSTAGE = NSTAGE_RAW > 4 ? 4 : NSTAGE_RAW;
   static constexpr int OFF_SC = NSTAGE * STAGE_BYTES;
-  static constexpr int OFF_BAR = OFF_SC + 2 * SC_BYTES;
+  static constexpr int OFF_BAR = OFF_SC + NSCB * SC_BYTES;
   static constexpr int OFF_MISC = OFF_BAR + BAR_BYTES;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   static_assert(NSTAGE >= 3, "pipeline too shallow");
   static_assert(SMEM_BYTES <= 232448, "shared memory over the sm_100 limit");
   static_assert(NPAIR * KS * BN <= TMEM_COLS, "TMEM buffers");
-  static_assert(2 * NSTAGE + 2 * NPAIR + 1 + 4 + 1 <= BAR_BYTES / 8, "barrier area");
+  static_assert(2 * NSTAGE + 2 * NPAIR + 2 + 2 * NSCB + 1 <= BAR_BYTES / 8, "barrier area");
+  static_assert(SC_BYTES % 128 == 0, "scale buffers are TMA destinations");
   static_assert(4 * BM * 4 <= SC_BYTES, "the amax exchange reuses a scale buffer");
 };
 
@@ -81,15 +87,15 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm_rows(const __gri
   constexpr int NSTAGE = C::NSTAGE, NPAIR = C::NPAIR, BM = C::BM, BN = C::BN, KS = C::KS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* scb = reinterpret_cast<float*>(smem + C::OFF_SC);  // [2][SC_FLOATS]
+  float* scb = reinterpret_cast<float*>(smem + C::OFF_SC);  // [NSCB][SC_FLOATS]
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* empty = full + NSTAGE;
   uint64_t* accf = empty + NSTAGE;
   uint64_t* acce = accf + NPAIR;
-  uint64_t* drain = acce + NPAIR;
-  uint64_t* sc_full = drain + 1;    // [2] the tile's scales landed
-  uint64_t* sc_free = sc_full + 2;  // [2] the epilogue is done with them
-  uint64_t* eall = sc_free + 2;     // EPI 1: all epilogue warps meet
+  uint64_t* drain = acce + NPAIR;   // [2] one per issuer
+  uint64_t* sc_full = drain + 2;         // [NSCB] the tile's scales landed
+  uint64_t* sc_free = sc_full + C::NSCB;  // [NSCB] the epilogue is done with them
+  uint64_t* eall = sc_free + C::NSCB;     // EPI 1: all epilogue warps meet
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
 
@@ -105,8 +111,8 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm_rows(const __gri
       mbar_init(&accf[b], 1);
       mbar_init(&acce[b], 4 * C::NWG);
     }
-    mbar_init(drain, 1);
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < 2; ++b) mbar_init(&drain[b], 1);
+    for (int b = 0; b < C::NSCB; ++b) {
       mbar_init(&sc_full[b], 1);
       mbar_init(&sc_free[b], 4 * C::NWG);
     }
@@ -129,26 +135,11 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm_rows(const __gri
   if (warp == 0) {
     // ───────────── TMA producer ─────────────
     Ring<NSTAGE> st;
-    uint32_t issued = 0, tcount = 0, sc_issued = 0;
+    uint32_t issued = 0;
     bool alive = true;
-    for (int tile = blockIdx.x; tile < ntiles && alive; tile += gridDim.x, ++tcount) {
+    for (int tile = blockIdx.x; tile < ntiles && alive; tile += gridDim.x) {
       const int4 td = args.tiles[tile];
       const int set = td.z >> 24, e = td.z & 0xFFFFFF;
-      const int sb = tcount & 1;
-      // the tile's scales: activation scales of rows (row0 & ~3) .. +131 for every K block,
-      // and the weight block's scale row(s)
-      if (!mbar_wait(&sc_free[sb], ((tcount >> 1) & 1) ^ 1, s_abort)) break;
-      if (lane == 0) {
-        float* sc = scb + sb * C::SC_FLOATS;
-        const uint32_t wbytes = (uint32_t)nkb * 4u;
-        mbar_arrive_expect_tx(&sc_full[sb], (uint32_t)C::SC_LD * wbytes + (uint32_t)C::NHALF * wbytes);
-        tma_load_2d(sc, &args.tmAS, &sc_full[sb], td.x & ~3, 0);
-        const int wrow = e * args.ws_rows[set] + td.w;
-        tma_load_2d(sc + C::SC_LD * C::MAXKB, &args.tmWS[set][0], &sc_full[sb], 0, wrow);
-        if constexpr (C::EPI == 1)
-          tma_load_2d(sc + C::SC_LD * C::MAXKB + C::MAXKB, &args.tmWS[set][1], &sc_full[sb], 0, wrow);
-      }
-      ++sc_issued;
       for (int s = 0; s < nsteps; ++s) {
         const int k0 = s * KS;
         const int h = k0 / nkb, kb = k0 - h * nkb;
@@ -159,18 +150,19 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm_rows(const __gri
         if (lane == 0) {
           uint8_t* sp = smem + st.i * C::STAGE_BYTES;
           mbar_arrive_expect_tx(&full[st.i], C::STAGE_BYTES);
+          // KS token tiles in one 3-D box: [kb][row][128 B]
+          tma_load_3d(sp, &args.tmTok, &full[st.i], 0, td.x, kb);
+          uint8_t* wp = sp + KS * C::KB_BYTES;
+          if constexpr (C::EPI == 1) {
+            // per K block: 64 gate rows then 64 up rows of the same channels (one 128-row operand)
+            const int r = e * args.w_rows[set] + td.w * 128 + h * 64;
 #pragma unroll
-          for (int j = 0; j < KS; ++j) {
-            const int x = (kb + j) * 128;
-            tma_load_2d(sp + j * C::KB_BYTES, &args.tmTok, &full[st.i], x, td.x);
-            uint8_t* wp = sp + (KS + j) * C::KB_BYTES;
-            if constexpr (C::EPI == 1) {
-              const int r = e * args.w_rows[set] + td.w * 128 + h * 64;
-              tma_load_2d(wp, &args.tmW[set][0], &full[st.i], x, r);
-              tma_load_2d(wp + 64 * 128, &args.tmW[set][1], &full[st.i], x, r);
-            } else {
-              tma_load_2d(wp, &args.tmW[set][0], &full[st.i], x, e * args.w_rows[set] + td.w * 128);
+            for (int j = 0; j < KS; ++j) {
+              tma_load_2d(wp + j * C::KB_BYTES, &args.tmW[set][0], &full[st.i], (kb + j) * 128, r);
+              tma_load_2d(wp + j * C::KB_BYTES + 64 * 128, &args.tmW[set][1], &full[st.i], (kb + j) * 128, r);
             }
+          } else {
+            tma_load_3d(wp, &args.tmW[set][0], &full[st.i], 0, e * args.w_rows[set] + td.w * 128, kb);
           }
         }
         __syncwarp();
@@ -182,18 +174,19 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm_rows(const __gri
     if (lane == 0) {
       const uint32_t first = issued > (uint32_t)NSTAGE ? issued - NSTAGE : 0;
       for (uint32_t q = first; q < issued; ++q) wait_plain(&full[q % NSTAGE], (q / NSTAGE) & 1, kWaitTimeoutNs);
-      for (uint32_t t = sc_issued > 2 ? sc_issued - 2 : 0; t < sc_issued; ++t)
-        wait_plain(&sc_full[t & 1], (t >> 1) & 1, kWaitTimeoutNs);
     }
     __syncwarp();
-  } else if (warp == 1) {
-    // ───────────── MMA issuer: KS K blocks per stage into one TMEM buffer pair ─────────────
+  } else if (warp == 1 || warp == 2) {
+    // ───────────── MMA issuers: KS K blocks per stage into one TMEM buffer pair; issuer i
+    // takes the stages that use pair i ─────────────
+    const int me = warp - 1;
     Ring<NSTAGE> st;
     Ring<NPAIR> bp;
     bool alive = true;
     const uint32_t idesc = umma_idesc_e4m3(BM, BN);
     for (int tile = blockIdx.x; tile < ntiles && alive; tile += gridDim.x) {
       for (int s = 0; s < nsteps; ++s, st.next(), bp.next()) {
+        if (bp.i != me) continue;
         if (!mbar_wait(&acce[bp.i], bp.ph ^ 1, s_abort) || !mbar_wait(&full[st.i], st.ph, s_abort)) {
           alive = false;
           break;
@@ -215,14 +208,41 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm_rows(const __gri
         __syncwarp();
       }
     }
+    // every MMA of this issuer must have completed before TMEM is released
     if (lane == 0) {
-      umma_commit(drain);
-      wait_plain(drain, 0, kWaitTimeoutNs);
+      umma_commit(&drain[me]);
+      wait_plain(&drain[me], 0, kWaitTimeoutNs);
     }
+    __syncwarp();
+  } else if (warp == 3) {
+    // ───────────── scales of each tile: activation scales of rows (row0 & ~3) .. +131 for
+    // every K block, and the weight block's scale row(s) ─────────────
+    uint32_t tcount = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tcount) {
+      const int sb = tcount % C::NSCB;
+      if (!mbar_wait(&sc_free[sb], ((tcount / C::NSCB) & 1) ^ 1, s_abort)) break;
+      if (lane == 0) {
+        const int4 td = args.tiles[tile];
+        const int set = td.z >> 24, e = td.z & 0xFFFFFF;
+        float* sc = scb + sb * C::SC_FLOATS;
+        const uint32_t wbytes = (uint32_t)nkb * 4u;
+        mbar_arrive_expect_tx(&sc_full[sb], (uint32_t)C::SC_LD * wbytes + (uint32_t)C::NHALF * wbytes);
+        tma_load_2d(sc, &args.tmAS, &sc_full[sb], td.x & ~3, 0);
+        const int wrow = e * args.ws_rows[set] + td.w;
+        tma_load_2d(sc + C::SC_LD * C::MAXKB, &args.tmWS[set][0], &sc_full[sb], 0, wrow);
+        if constexpr (C::EPI == 1)
+          tma_load_2d(sc + C::SC_LD * C::MAXKB + C::MAXKB, &args.tmWS[set][1], &sc_full[sb], 0, wrow);
+      }
+      __syncwarp();
+    }
+    // no copy into this CTA's shared memory may outlive the CTA
+    if (lane == 0)
+      for (uint32_t t = tcount > (uint32_t)C::NSCB ? tcount - C::NSCB : 0; t < tcount; ++t)
+        wait_plain(&sc_full[t % C::NSCB], (t / C::NSCB) & 1, kWaitTimeoutNs);
     __syncwarp();
   } else {
     // ───────────── epilogue: 16 warps, TMEM lane = token row ─────────────
-    const int ew = warp - 2, wg = ew >> 2, q = warp & 3;
+    const int ew = warp - C::NCTRL, wg = ew >> 2, q = warp & 3;
     const int lrow = q * 32 + lane;
     const uint32_t tlane = (uint32_t)(q * 32) << 16;
     Ring<NPAIR> bp;
@@ -239,8 +259,8 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm_rows(const __gri
       const int4 td = args.tiles[tile];
       const int nr = td.y;
       const int64_t row0 = td.x;
-      const int sb = tcount & 1;
-      if (!mbar_wait(&sc_full[sb], (tcount >> 1) & 1, s_abort)) break;
+      const int sb = tcount % C::NSCB;
+      if (!mbar_wait(&sc_full[sb], (tcount / C::NSCB) & 1, s_abort)) break;
       float* sc = scb + sb * C::SC_FLOATS;
       const float* a_s = sc + (int)(row0 & 3) + lrow;  // a_s[kb * SC_LD]
       const float* w_s = sc + C::SC_LD * C::MAXKB;       // gate [0, MAXKB), up [MAXKB, 2 MAXKB)
