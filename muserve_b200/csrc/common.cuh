@@ -251,111 +251,4 @@ MSV_DEVICE void cp_async_mbar_arrive(uint64_t* bar) {
 }
 MSV_DEVICE void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-// ── CTA pairs (2-CTA clusters sharing one tcgen05 MMA) ──────────────────────────────────
-// Rank 0 of the pair issues every MMA; its operands and TMEM accumulators are split over the
-// two SMs (A by rows, B by columns, D by rows).  Shared-memory layouts are identical in both
-// CTAs, so one descriptor addresses both halves.
-
-MSV_DEVICE uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-// Address of the same shared-memory offset in CTA `rank` of this cluster.
-MSV_DEVICE uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
-// All threads of both CTAs; orders barrier initialisation (and everything else) across the pair.
-MSV_DEVICE void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// Arrive on a barrier of either CTA of the pair.  `_cluster` orders this thread's earlier
-// memory writes for the peer (data handed over through shared memory); `_remote` is the
-// plain form for pipeline barriers whose payload is ordered by tcgen05 fences or TMA.
-MSV_DEVICE void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-MSV_DEVICE void mbar_arrive_remote(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-MSV_DEVICE bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-MSV_DEVICE bool mbar_try_wait_cluster_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait on a barrier whose arrivals hand over data written by the peer CTA
-// (cluster-scope acquire).
-MSV_DEVICE bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
-  const long long t0 = clock64();
-  for (;;) {
-    if (mbar_try_wait_cluster_sleep(bar, parity, kSuspendNs)) return true;
-    if (*abort) return false;
-    if (clock64() - t0 > kWaitTimeoutCycles) {
-      *abort = 1;
-      return false;
-    }
-  }
-}
-// 2-D tiled load into this CTA's shared memory whose completion is counted on the barrier
-// at `bar_cluster` (a cluster address: rank 0's barrier), no multicast.
-MSV_DEVICE void tma_load_2d_pair(void* dst, const CUtensorMap* m, uint32_t bar_cluster, int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
-      "[%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar_cluster), "r"(x), "r"(y)
-      : "memory");
-}
-// M = 256 MMA over the pair (rank 0 issues): A rows 0-127 from rank 0's tile, 128-255 from
-// rank 1's; B columns split in halves the same way; D rows land in each SM's own TMEM.
-MSV_DEVICE void umma_f8_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accum) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, {%5, %6, %7, %8, %9, %10, %11, %12}, p;\n\t}" ::"r"(
-          tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u),
-      "r"(0u));
-}
-// Arrive on the barrier at this shared-memory offset in every CTA of `cta_mask` once the
-// pair MMAs issued so far have completed.
-MSV_DEVICE void umma_commit_pair(uint64_t* bar, uint16_t cta_mask) {
-  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-                   smem_u32(bar)),
-               "h"(cta_mask)
-               : "memory");
-}
-// Warp-wide, the same warp in both CTAs: TMEM columns for pair MMAs.
-MSV_DEVICE void tmem_alloc_pair(uint32_t* dst, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)),
-               "r"(ncols)
-               : "memory");
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-MSV_DEVICE void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-MSV_DEVICE void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
-  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
-}
-
 }  // namespace msv
