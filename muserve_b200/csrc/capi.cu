@@ -573,7 +573,7 @@ int msv_gemm_fp8_nt_groupwise(const uint8_t* a, const float* a_scale, int M, int
 namespace {
 struct LayerPlan {
   int T, H, E, k, I, Is, P, rows, e_local;
-  bool shared, small1, small2, rows1, rows2;
+  bool shared, small1, small2, rows1, rows2, gather;
   int bn1, bn2, nb1, nb2, srows;
   size_t cap1, cap2;
 };
@@ -612,6 +612,8 @@ int plan_layer(const msv_moe_shape* s, LayerPlan* L) {
   L->nb1 = L->I / 128;
   L->nb2 = L->H / 128;
   L->srows = (L->rows + 3) & ~3;  // K-block stride of the activation scales (16-byte rows)
+  // large batches quantise each token once and gather the e4m3 rows (16-byte scale rows)
+  L->gather = L->P > kPermSingleMax && (L->H / 128) % 4 == 0;
   L->cap1 = tile_cap(L->e_local, L->P, L->bn1, L->nb1) + (size_t)L->nb1 * ((L->T + L->bn1 - 1) / L->bn1 + 1);
   L->cap2 = tile_cap(L->e_local, L->P, L->bn2, L->nb2) + (size_t)L->nb2 * ((L->T + L->bn2 - 1) / L->bn2 + 1);
   return MSV_OK;
@@ -621,9 +623,10 @@ struct LayerWs {
   int32_t *ids, *counts, *num_local, *slot_row, *row_token;
   void* w;
   int4 *tiles1, *tiles2;
+  int *blk_hist, *blk_nloc, *lrank, *lpos;  // multi-block dispatch scratch
   int *ntiles1, *ntiles2;
-  uint8_t *xq, *aq;
-  float *xs, *as, *gate_val;
+  uint8_t *xq, *aq, *xq_tok;
+  float *xs, *as, *gate_val, *xs_tok;
   __nv_bfloat16* down;
 };
 
@@ -645,6 +648,13 @@ size_t carve_layer(const LayerPlan& L, uint8_t* base, LayerWs* w) {
   w->as = c.take<float>((size_t)L.srows * (L.I / 128));
   w->down = c.take<__nv_bfloat16>((size_t)L.rows * L.H);
   w->gate_val = c.take<float>((size_t)(L.T > 0 ? L.T : 1));
+  const int nblk = (L.P + kPermThreads - 1) / kPermThreads;
+  w->blk_hist = c.take<int>((size_t)(nblk > 0 ? nblk : 1) * L.e_local);
+  w->blk_nloc = c.take<int>((size_t)(nblk > 0 ? nblk : 1));
+  w->lrank = c.take<int>((size_t)(L.P > 0 ? L.P : 1));
+  w->lpos = c.take<int>((size_t)(L.P > 0 ? L.P : 1));
+  w->xq_tok = L.gather ? c.take<uint8_t>((size_t)L.T * L.H) : nullptr;
+  w->xs_tok = L.gather ? c.take<float>((size_t)L.T * (L.H / 128)) : nullptr;
   return c.off + 256;
 }
 }  // namespace
@@ -723,33 +733,79 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
   const bool do_shared = L.shared && s->add_shared;  // ranks that do not add it skip its GEMMs
   p.shared_rows = do_shared ? L.T : 0;
   p.row_base_shared = L.P;
-  const size_t psm = permute_smem_bytes(L.e_local);
-  if (psm > 48 * 1024)
-    if (int rc = cuda_check(cudaFuncSetAttribute(k_permute, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psm),
-                            "cudaFuncSetAttribute(permute)"))
-      return rc;
   if (int rc = mark(1)) return rc;
-  k_permute<<<1, kPermThreads, psm, stream>>>(p);
-  if (int rc = cuda_check(cudaGetLastError(), "launch permute")) return rc;
+  if (L.P <= kPermSingleMax) {
+    // one block: the whole stable counting sort and the tile lists
+    const size_t psm = permute_smem_bytes(L.e_local);
+    if (psm > 48 * 1024)
+      if (int rc = cuda_check(cudaFuncSetAttribute(k_permute, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psm),
+                              "cudaFuncSetAttribute(permute)"))
+        return rc;
+    k_permute<<<1, kPermThreads, psm, stream>>>(p);
+    if (int rc = cuda_check(cudaGetLastError(), "launch permute")) return rc;
+  } else {
+    // the same sort over blocks of slots: counts, one scan block (+ tile lists), scatter
+    PermuteScratch ps{w.blk_hist, w.blk_nloc, w.lrank, w.lpos, (L.P + kPermThreads - 1) / kPermThreads};
+    const size_t csm = perm_count_smem_bytes(L.e_local);
+    if (csm > 48 * 1024)
+      if (int rc = cuda_check(cudaFuncSetAttribute(k_perm_count, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csm),
+                              "cudaFuncSetAttribute(perm_count)"))
+        return rc;
+    k_perm_count<<<ps.nblk, kPermThreads, csm, stream>>>(p, ps);
+    if (int rc = cuda_check(cudaGetLastError(), "launch perm_count")) return rc;
+    k_perm_scan<<<1, kPermThreads, perm_scan_smem_bytes(L.e_local), stream>>>(p, ps);
+    if (int rc = cuda_check(cudaGetLastError(), "launch perm_scan")) return rc;
+    k_perm_scatter<<<(L.P + 255) / 256, 256, 0, stream>>>(p, ps);
+    if (int rc = cuda_check(cudaGetLastError(), "launch perm_scatter")) return rc;
+  }
   if (int rc = mark(2)) return rc;
   // 3. gather + quantise (routed rows in expert order, then the shared expert's rows)
   QuantArgs q{};
   q.x = static_cast<const __nv_bfloat16*>(hidden);
   q.ldx = L.H;
   q.K = L.H;
-  q.rows_a = L.P;
-  q.idx_a = w.row_token;
-  q.nvalid_a = w.num_local;
-  q.rows_b = do_shared ? L.T : 0;
-  q.q = w.xq;
-  q.ldq = L.H;
-  q.scale = w.xs;
-  q.s_row = 1;
-  q.s_kb = L.srows;
   q.gate_w = (do_shared && W->sh_gate_logit_w) ? static_cast<const __nv_bfloat16*>(W->sh_gate_logit_w) : nullptr;
   q.gate_val = w.gate_val;
-  k_quant_rows<<<(L.rows + kQuantWarps - 1) / kQuantWarps, kQuantWarps * 32, 0, stream>>>(q);
-  if (int rc = cuda_check(cudaGetLastError(), "launch quant")) return rc;
+  if (L.gather) {
+    // every token once, in token order (segment B computes the shared-expert gate too) ...
+    q.rows_a = 0;
+    q.rows_b = L.T;
+    q.q = w.xq_tok;
+    q.ldq = L.H;
+    q.scale = w.xs_tok;
+    q.s_row = L.H / 128;
+    q.s_kb = 1;
+    if (!do_shared) q.gate_w = nullptr;
+    k_quant_rows<<<(L.T + kQuantWarps - 1) / kQuantWarps, kQuantWarps * 32, 0, stream>>>(q);
+    if (int rc = cuda_check(cudaGetLastError(), "launch quant")) return rc;
+    // ... then the routed (and shared-expert) rows copied into expert-sorted order
+    GatherArgs g{};
+    g.qt = w.xq_tok;
+    g.st = w.xs_tok;
+    g.K = L.H;
+    g.rows_a = L.P;
+    g.row_token = w.row_token;
+    g.nvalid = w.num_local;
+    g.rows_b = do_shared ? L.T : 0;
+    g.q = w.xq;
+    g.scale = w.xs;
+    g.s_kb = L.srows;
+    const int gwarps = (L.rows + 31) / 32;
+    k_gather_rows<<<(gwarps + kGatherWarps - 1) / kGatherWarps, kGatherWarps * 32, 0, stream>>>(g);
+    if (int rc = cuda_check(cudaGetLastError(), "launch gather")) return rc;
+  } else {
+    q.rows_a = L.P;
+    q.idx_a = w.row_token;
+    q.nvalid_a = w.num_local;
+    q.rows_b = do_shared ? L.T : 0;
+    q.q = w.xq;
+    q.ldq = L.H;
+    q.scale = w.xs;
+    q.s_row = 1;
+    q.s_kb = L.srows;
+    k_quant_rows<<<(L.rows + kQuantWarps - 1) / kQuantWarps, kQuantWarps * 32, 0, stream>>>(q);
+    if (int rc = cuda_check(cudaGetLastError(), "launch quant")) return rc;
+  }
   if (int rc = mark(3)) return rc;
   // 4. gate_up GEMM with SwiGLU + requant epilogue
   const uint64_t gu_rows = (uint64_t)(L.e_local - 1) * W->gu_expert_rows + L.I;
@@ -903,7 +959,7 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
   cb.gate_val = (do_shared && W->sh_gate_logit_w) ? w.gate_val : nullptr;
   cb.out = static_cast<__nv_bfloat16*>(out);
   cb.ld_out = L.H;
-  k_combine<<<L.T, kCombineThreads, 0, stream>>>(cb);
+  launch_combine(cb, stream);
   if (int rc = cuda_check(cudaGetLastError(), "launch combine")) return rc;
   return mark(6);
 }

@@ -15,6 +15,11 @@
 
 namespace msv {
 
+// element `hi` (0: low half, 1: high half) of two packed bf16 values, widened exactly to f32
+__device__ __forceinline__ float bf16_bits_to_f32(uint32_t w, int hi) {
+  return __uint_as_float(hi ? (w & 0xffff0000u) : (w << 16));
+}
+
 // Every device-side wait gives up after this long and reports MSV_ERR_TIMEOUT through the
 // kernel's error word; nothing in these kernels can spin forever.  Hot-path waits count SM
 // cycles (clock64, cheap to read); 4e9 cycles is about 2 s at the B200's 1.97 GHz.

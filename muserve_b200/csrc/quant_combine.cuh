@@ -102,6 +102,73 @@ __global__ void __launch_bounds__(kQuantWarps * 32) k_quant_rows(QuantArgs a) {
   }
 }
 
+// Large batches quantise every token once (k_quant_rows over the T token rows, into a
+// token-ordered buffer) and then copy the e4m3 rows and their scales into the expert-sorted
+// order the GEMMs read: a token's 128-channel blocks quantise the same way in every expert it
+// is routed to, so this equals quantising each gathered row, with one eleventh of the
+// arithmetic and HBM reads of the per-row form.
+struct GatherArgs {
+  const uint8_t* qt;       // [T, K] e4m3, token order
+  const float* st;         // [T, K/128] scales, token order
+  int K;
+  int rows_a;              // routed rows [0, rows_a) read token row_token[r]; rows at or
+  const int32_t* row_token;  // beyond *nvalid are skipped
+  const int32_t* nvalid;
+  int rows_b;              // shared-expert rows [rows_a, rows_a + rows_b) read token r - rows_a
+  uint8_t* q;              // [rows, K] e4m3, sorted order
+  float* scale;            // element (r, kb) at scale[kb * s_kb + r]
+  int64_t s_kb;
+};
+
+constexpr int kGatherWarps = 8;
+
+// A warp moves 32 consecutive rows: each row's bytes with 16-byte lanes, then the 32 rows'
+// scales one K block at a time (lane = row, so each K block is one coalesced store).
+__global__ void __launch_bounds__(kGatherWarps * 32) k_gather_rows(GatherArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int r0 = (blockIdx.x * kGatherWarps + (threadIdx.x >> 5)) * 32;
+  const int rows = a.rows_a + a.rows_b;
+  if (r0 >= rows) return;
+  const int nvalid = a.nvalid ? *a.nvalid : a.rows_a;
+  // source token of row r0 + lane (-1: skip)
+  int tok = -1;
+  const int rl = r0 + lane;
+  if (rl < a.rows_a) tok = rl < nvalid ? a.row_token[rl] : -1;
+  else if (rl < rows) tok = rl - a.rows_a;
+  const int n16 = a.K / 16;  // 16-byte chunks per row
+  for (int i = 0; i < 32; ++i) {
+    const int t = __shfl_sync(0xffffffffu, tok, i);
+    if (t < 0) continue;
+    const uint4* __restrict__ src = reinterpret_cast<const uint4*>(a.qt + (int64_t)t * a.K);
+    uint4* __restrict__ dst = reinterpret_cast<uint4*>(a.q + (int64_t)(r0 + i) * a.K);
+    for (int c0 = 0; c0 < n16; c0 += 32 * 8) {
+      uint4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < n16) v[u] = src[c];
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < n16) dst[c] = v[u];
+      }
+    }
+  }
+  // scales: K/128 is a multiple of 4 on this path (16-byte rows of token scales)
+  const int nkb = a.K / 128;
+  if (tok >= 0) {
+    const float4* sp = reinterpret_cast<const float4*>(a.st + (int64_t)tok * nkb);
+    for (int kb = 0; kb < nkb; kb += 4) {
+      const float4 v = sp[kb / 4];
+      a.scale[(int64_t)(kb + 0) * a.s_kb + rl] = v.x;
+      a.scale[(int64_t)(kb + 1) * a.s_kb + rl] = v.y;
+      a.scale[(int64_t)(kb + 2) * a.s_kb + rl] = v.z;
+      a.scale[(int64_t)(kb + 3) * a.s_kb + rl] = v.w;
+    }
+  }
+}
+
 struct CombineArgs {
   const __nv_bfloat16* down;  // [rows, H] expert outputs in sorted-row order
   int64_t ld_down;
@@ -119,12 +186,19 @@ struct CombineArgs {
   int64_t ld_out;
 };
 
-constexpr int kCombineThreads = 256;
+constexpr int kCombineThreads = 512;  // most threads a CTA is launched with
+constexpr int kCombineBatch = 8;  // slot rows loaded before any is summed
 
-// One CTA per token; each thread produces 8 consecutive channels per pass.  Warp 0 reads
-// the token's k slots in parallel (and orders them by expert id for the per-expert modes);
-// the channel loop keeps 4 slot rows in flight at a time.
-__global__ void __launch_bounds__(kCombineThreads) k_combine(CombineArgs a) {
+inline int combine_threads(int H) {
+  const int t = ((H / 8 + 31) / 32) * 32;
+  return t < kCombineThreads ? t : kCombineThreads;
+}
+
+// One CTA per token; each thread produces 8 consecutive channels per pass (one pass when
+// H <= 4096).  Warp 0 reads the token's k slots in parallel (and orders them by expert id for
+// the per-expert modes); the channel loop loads 8 slot rows before it sums them.
+template <int MODE>
+__global__ void __launch_bounds__(kCombineThreads, 2) k_combine(CombineArgs a) {
   const int t = blockIdx.x;
   __shared__ int s_row[16];
   __shared__ float s_w[16];
@@ -140,7 +214,7 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(CombineArgs a) {
       id = a.topk_ids ? a.topk_ids[o] : j;
     }
     int pos = j;
-    if (a.mode != MSV_COMBINE_V2) {  // expert-ascending order of the per-expert loops
+    if (MODE != MSV_COMBINE_V2) {  // expert-ascending order of the per-expert loops
       pos = 0;
       for (int i = 0; i < a.k; ++i) {
         const int idi = __shfl_sync(0xffffffffu, id, i);
@@ -154,50 +228,63 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(CombineArgs a) {
   }
   __syncthreads();
   const float gv = (a.add_shared && a.gate_val) ? a.gate_val[t] : 1.0f;
-  for (int c = threadIdx.x * 8; c < a.H; c += kCombineThreads * 8) {
+  for (int c = threadIdx.x * 8; c < a.H; c += blockDim.x * 8) {
     float acc[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-    for (int j0 = 0; j0 < a.k; j0 += 4) {
-      uint4 raw[4];
+    // kCombineBatch slot rows in flight at once (the shared-expert row with the first batch),
+    // summed in slot order
+    uint4 rsh = make_uint4(0, 0, 0, 0);
+    for (int j0 = 0; j0 < a.k; j0 += kCombineBatch) {
+      uint4 raw[kCombineBatch];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int r = (j0 + u < a.k) ? s_row[j0 + u] : -1;
+      for (int u = 0; u < kCombineBatch; ++u) {
+        const int r = j0 + u < a.k ? s_row[j0 + u] : -1;
         raw[u] = r >= 0 ? *reinterpret_cast<const uint4*>(a.down + (int64_t)r * a.ld_down + c) : make_uint4(0, 0, 0, 0);
       }
+      if (j0 == 0 && a.add_shared)
+        rsh = *reinterpret_cast<const uint4*>(a.down + (int64_t)(a.shared_row0 + t) * a.ld_down + c);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < kCombineBatch; ++u) {
         const int j = j0 + u;
         if (j >= a.k) break;
         if (s_row[j] < 0) continue;
         const float w = s_w[j];
-        const __nv_bfloat16* d = reinterpret_cast<const __nv_bfloat16*>(&raw[u]);
+        const uint32_t wd[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const float dv = __bfloat162float(d[i]);
-          if (a.mode == MSV_COMBINE_V2) acc[i] += bf16_round(dv * w);
+          const float dv = bf16_bits_to_f32(wd[i >> 1], i & 1);
+          if (MODE == MSV_COMBINE_V2) acc[i] += bf16_round(dv * w);
           // fp32 product and fp32 add rounded separately (no FMA contraction), then bf16
-          else if (a.mode == MSV_COMBINE_DISPATCH) acc[i] = bf16_round(__fadd_rn(acc[i], __fmul_rn(dv, w)));
+          else if (MODE == MSV_COMBINE_DISPATCH) acc[i] = bf16_round(__fadd_rn(acc[i], __fmul_rn(dv, w)));
           else acc[i] = bf16_round(acc[i] + bf16_round(dv * w));
         }
       }
     }
     if (a.add_shared) {
-      uint4 raw = *reinterpret_cast<const uint4*>(a.down + (int64_t)(a.shared_row0 + t) * a.ld_down + c);
-      const __nv_bfloat16* d = reinterpret_cast<const __nv_bfloat16*>(&raw);
+      const uint32_t wd[4] = {rsh.x, rsh.y, rsh.z, rsh.w};
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        float sd = __bfloat162float(d[i]);
+        float sd = bf16_bits_to_f32(wd[i >> 1], i & 1);
         if (a.gate_val) sd = bf16_round(sd * gv);
         acc[i] = bf16_round(bf16_round(acc[i]) + sd);
       }
     }
-    uint4 o;
-    __nv_bfloat16* oh = reinterpret_cast<__nv_bfloat16*>(&o);
+    uint32_t ow[4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) oh[i] = __float2bfloat16_rn(acc[i]);
-    *reinterpret_cast<uint4*>(a.out + (int64_t)t * a.ld_out + c) = o;
+    for (int i = 0; i < 4; ++i) {
+      const __nv_bfloat162 p = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+      ow[i] = *reinterpret_cast<const uint32_t*>(&p);
+    }
+    *reinterpret_cast<uint4*>(a.out + (int64_t)t * a.ld_out + c) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
   }
+}
+
+inline void launch_combine(const CombineArgs& a, cudaStream_t stream) {
+  const dim3 grid(a.T), block(combine_threads(a.H));
+  if (a.mode == MSV_COMBINE_V2) k_combine<MSV_COMBINE_V2><<<grid, block, 0, stream>>>(a);
+  else if (a.mode == MSV_COMBINE_DISPATCH) k_combine<MSV_COMBINE_DISPATCH><<<grid, block, 0, stream>>>(a);
+  else k_combine<MSV_COMBINE_BATCHED><<<grid, block, 0, stream>>>(a);
 }
 
 }  // namespace msv

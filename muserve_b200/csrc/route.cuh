@@ -337,6 +337,7 @@ struct PermuteArgs {
 
 constexpr int kPermThreads = 1024;
 constexpr int kPermWarps = kPermThreads / 32;
+constexpr int kPermSingleMax = 8192;  // above this many slots the dispatch runs over many blocks
 
 MSV_DEVICE int load_id(const PermuteArgs& p, int f) {
   return p.ids_i64 ? (int)reinterpret_cast<const int64_t*>(p.ids)[f] : reinterpret_cast<const int32_t*>(p.ids)[f];
@@ -512,6 +513,143 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermuteArgs p) {
 }
 
 size_t permute_smem_bytes(int e_local) { return (size_t)(kPermWarps * e_local + 3 * e_local + 1) * sizeof(int); }
+
+// ── multi-block dispatch (large T*k) ──────────────────────────────────────────────────────
+// The same stable counting sort as k_permute, spread over blocks of kPermThreads slots:
+//   k_perm_count:   per block, each slot's rank among the block's earlier slots of its expert
+//                   (warp match + per-warp counts) and its index among the block's local slots;
+//                   the block's per-expert counts and local count.
+//   k_perm_scan:    one block: per-expert totals and offsets, every block's base per expert
+//                   (offset + counts of earlier blocks), counts / num_local / tile lists.
+//   k_perm_scatter: row = block base[expert] + rank; the slot <-> row maps.
+// Slot f goes to block f / kPermThreads, warp (f % kPermThreads) / 32, lane f % 32, so the
+// order (block, warp, lane) is slot order and the sort is stable as torch's argsort(stable).
+struct PermuteScratch {
+  int* blk_hist;  // [nblk][e_local] block counts, then block bases
+  int* blk_nloc;  // [nblk] local slots per block, then their exclusive prefix
+  int* lrank;     // [T*k] rank within (block, expert), -1 when not local
+  int* lpos;      // [T*k] index among the block's local slots
+  int nblk;
+};
+
+size_t perm_count_smem_bytes(int e_local) { return (size_t)(kPermWarps * e_local) * sizeof(int); }
+
+__global__ void __launch_bounds__(kPermThreads) k_perm_count(PermuteArgs p, PermuteScratch s) {
+  extern __shared__ __align__(16) int wc[];  // [kPermWarps][e_local] per-warp counts, then bases
+  __shared__ int s_wn[kPermWarps + 1];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int E = p.e_local;
+  const int P = p.T * p.k;
+  const int f = blockIdx.x * kPermThreads + threadIdx.x;
+  for (int i = threadIdx.x; i < kPermWarps * E; i += kPermThreads) wc[i] = 0;
+  __syncthreads();
+  const bool valid = f < P;
+  const int e = valid ? load_id(p, f) : -1;
+  const int le = p.placement == 0 ? e : (e >= 0 ? e / p.tp : -1);
+  const bool local = valid && (p.placement == 0 || (e % p.tp) == p.rank) && le >= 0 && le < E;
+  const uint32_t bal = __ballot_sync(0xffffffffu, local);
+  const uint32_t peers = __match_any_sync(0xffffffffu, local ? (uint32_t)le : 0xffffffffu);
+  const int rank_w = __popc(peers & lanemask_lt());
+  if (local && (__ffs(peers) - 1) == lane) wc[warp * E + le] = __popc(peers);
+  if (lane == 0) s_wn[warp] = __popc(bal);
+  __syncthreads();
+  // per expert: exclusive scan over the warps (slot order), block total
+  for (int x = threadIdx.x; x < E; x += kPermThreads) {
+    int run = 0;
+    for (int w = 0; w < kPermWarps; ++w) {
+      const int c = wc[w * E + x];
+      wc[w * E + x] = run;
+      run += c;
+    }
+    s.blk_hist[blockIdx.x * E + x] = run;
+  }
+  if (warp == 0) {
+    const int v = s_wn[lane];
+    int incl = v;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    s_wn[lane] = incl - v;
+    if (lane == 31) s.blk_nloc[blockIdx.x] = incl;
+  }
+  __syncthreads();
+  if (valid) {
+    s.lrank[f] = local ? wc[warp * E + le] + rank_w : -1;
+    s.lpos[f] = local ? s_wn[warp] + __popc(bal & lanemask_lt()) : -1;
+  }
+}
+
+__global__ void __launch_bounds__(kPermThreads) k_perm_scan(PermuteArgs p, PermuteScratch s) {
+  extern __shared__ __align__(16) int scan_sm[];  // counts [E], offsets [E+1], scratch [E]
+  __shared__ int s_warp[33];
+  const int E = p.e_local;
+  int* counts = scan_sm;
+  int* offsets = counts + E;
+  int* scratch = offsets + E + 1;
+  for (int x = threadIdx.x; x < E; x += kPermThreads) {
+    int c = 0;
+    for (int b = 0; b < s.nblk; ++b) c += s.blk_hist[b * E + x];
+    counts[x] = c;
+  }
+  __syncthreads();
+  int total = 0;
+  const int off = block_excl_scan(threadIdx.x < E ? counts[threadIdx.x] : 0, s_warp, &total);
+  if (threadIdx.x < E) offsets[threadIdx.x] = off;
+  if (threadIdx.x == 0) {
+    offsets[E] = total;
+    *p.num_local = total;
+  }
+  __syncthreads();
+  for (int x = threadIdx.x; x < E; x += kPermThreads) {
+    int run = offsets[x];
+    for (int b = 0; b < s.nblk; ++b) {
+      const int c = s.blk_hist[b * E + x];
+      s.blk_hist[b * E + x] = run;
+      run += c;
+    }
+    if (p.expert_counts) p.expert_counts[x] = counts[x];
+  }
+  // exclusive prefix of the blocks' local counts
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int b = 0; b < s.nblk; ++b) {
+      const int c = s.blk_nloc[b];
+      s.blk_nloc[b] = run;
+      run += c;
+    }
+  }
+  if (p.sorted_expert_ids && p.alignment > 0) {
+    const int padded = ((total + p.alignment - 1) / p.alignment) * p.alignment;
+    for (int r = total + threadIdx.x; r < padded; r += kPermThreads) p.sorted_expert_ids[r] = -1;
+  }
+  __syncthreads();
+  if (p.tiles1) build_tiles(p, counts, offsets, scratch, s_warp, p.tiles1, p.ntiles1, p.bn1, p.nb1);
+  if (p.tiles2) build_tiles(p, counts, offsets, scratch, s_warp, p.tiles2, p.ntiles2, p.bn2, p.nb2);
+}
+
+size_t perm_scan_smem_bytes(int e_local) { return (size_t)(3 * e_local + 1) * sizeof(int); }
+
+__global__ void __launch_bounds__(256) k_perm_scatter(PermuteArgs p, PermuteScratch s) {
+  const int P = p.T * p.k;
+  const int f = blockIdx.x * blockDim.x + threadIdx.x;
+  if (f >= P) return;
+  const int lr = s.lrank[f];
+  if (lr < 0) {
+    if (p.slot_row) p.slot_row[f] = -1;
+    return;
+  }
+  const int e = load_id(p, f);
+  const int le = p.placement == 0 ? e : e / p.tp;
+  const int b = f / kPermThreads;
+  const int r = s.blk_hist[b * p.e_local + le] + lr;
+  const int lp = s.blk_nloc[b] + s.lpos[f];
+  if (p.slot_row) p.slot_row[f] = r;
+  if (p.row_token) p.row_token[r] = f / p.k;
+  if (p.sort_order) p.sort_order[r] = lp;
+  if (p.inverse_order) p.inverse_order[lp] = r;
+  if (p.sorted_expert_ids) p.sorted_expert_ids[r] = le;
+}
 
 // Groups from an arbitrary per-row expert array (the ragged-GEMM shim): every maximal run
 // of equal non-negative ids is one group, chunked by bn, times nb n-blocks.  One CTA.
