@@ -51,6 +51,25 @@ int msv_route_topk(const float* logits, int64_t ld_logits, int T, int E, int k, 
                    void* topk_w, int w_dtype, void* topk_ids, int ids_dtype, msv_stream_t stream);
 
 /*
+ * Router from the hidden states: logits = hidden @ gate_w^T on the tensor cores (bf16 x bf16,
+ * fp32 accumulation), then softmax / top-k / renormalisation exactly as msv_route_topk.
+ *   replaces: muserve/model/qwen35_layer_v2.py:567-572 (bf16_linear(hidden, gate_w).float(),
+ *             softmax, topk, renormalise; pass round_logits_bf16 = 1) and
+ *             muserve/kernels/moe_dispatch.py:8-24 (moe_gate: fp32 linear, softmax, topk,
+ *             renormalise; pass round_logits_bf16 = 0)
+ * hidden: [T,H] bf16 contiguous; gate_w: [E,H] bf16 contiguous; both 16-byte aligned.
+ * H % 64 == 0, 16 <= E <= 1024, E % 16 == 0, 1 <= k <= 16.
+ * round_logits_bf16: round each fp32 logit to bf16 before the softmax (the bf16 GEMM output).
+ * logits_out: optional [T,E] fp32, 16-byte aligned: the logits the routing used.
+ * workspace: >= msv_router_workspace_size(T, H, E) bytes, 256-byte aligned (fp32 partial sums
+ * of the K splits, summed in split order by a separate kernel: deterministic).
+ */
+size_t msv_router_workspace_size(int T, int H, int E);
+int msv_router_from_hidden(const void* hidden, const void* gate_w, int T, int H, int E, int k, int renormalize,
+                           int round_logits_bf16, void* topk_w, int w_dtype, void* topk_ids, int ids_dtype,
+                           float* logits_out, void* workspace, size_t workspace_bytes, msv_stream_t stream);
+
+/*
  * Top-k selection only, on given fp32 values (no softmax): torch.topk(values, k) order.
  *   replaces: the torch.topk call of muserve/model/qwen35_layer_v2.py:570
  * out_values may be NULL.

@@ -44,6 +44,8 @@ _SIGS = {
     "msv_check_device_error": (I, [P]),
     "msv_route_topk": (I, [P, I64, I, I, I, I, P, I, P, I, P]),
     "msv_topk_select": (I, [P, I64, I, I, I, P, I, P, P]),
+    "msv_router_workspace_size": (SZ, [I, I, I]),
+    "msv_router_from_hidden": (I, [P, P, I, I, I, I, I, I, P, I, P, I, P, P, SZ, P]),
     "msv_moe_permute": (I, [P, I, I, I, I, I, I, I, I, P, P, P, P, P, P]),
     "msv_fp8_quant_128": (I, [P, I64, I, I, P, P, I64, P, I64, I64, P]),
     "msv_ragged_gemm_workspace_size": (SZ, [I, I]),

@@ -13,6 +13,7 @@
 #include "grouped_gemm_rows.cuh"
 #include "quant_combine.cuh"
 #include "route.cuh"
+#include "router_gemm.cuh"
 
 namespace msv {
 
@@ -131,6 +132,39 @@ int tensor_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t cols,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(MSV_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d) rows=%llu cols=%llu", (int)r,
+                                     (unsigned long long)rows, (unsigned long long)cols);
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_maps.size() > 8192) g_maps.clear();
+  g_maps.emplace(key, m);
+  *out = m;
+  return MSV_OK;
+}
+
+// 2-D bf16 matrix [rows, cols] with row stride `stride` bytes, box [box_rows x 64 elements]
+// (128 bytes), 128-byte swizzle, zero fill out of bounds.  Cached like tensor_map.
+int tensor_map_bf16(CUtensorMap* out, const void* base, uint64_t rows, uint64_t cols, uint64_t stride, uint32_t box_rows) {
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return fail(MSV_ERR_INVALID, "bf16 operand not 16-byte aligned");
+  if (stride % 16 != 0 || cols % 64 != 0) return fail(MSV_ERR_INVALID, "bf16 operand row stride / width not multiple of 16 B / 64");
+  MapKey key{reinterpret_cast<uintptr_t>(base), rows, cols, stride, box_rows, 64, 3};
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_maps.find(key);
+    if (it != g_maps.end()) {
+      *out = it->second;
+      return MSV_OK;
+    }
+  }
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(MSV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {stride};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MSV_ERR_INVALID, "cuTensorMapEncodeTiled (bf16) failed (%d) rows=%llu cols=%llu", (int)r,
                                      (unsigned long long)rows, (unsigned long long)cols);
   std::lock_guard<std::mutex> lk(g_mu);
   if (g_maps.size() > 8192) g_maps.clear();
@@ -358,6 +392,91 @@ int msv_route_topk(const float* logits, int64_t ld, int T, int E, int k, int ren
   const size_t sm = route_smem_bytes(E);
   k_route_topk<<<(T + kRouteWarps - 1) / kRouteWarps, kRouteWarps * 32, sm, stream>>>(
       logits, ld, T, E, k, 1, renormalize, topk_w, w_dtype, topk_ids, ids_dtype, nullptr);
+  return cuda_check(cudaGetLastError(), "launch route_topk");
+}
+
+namespace {
+// K splits of the router GEMM: enough CTAs to cover the SMs when the token and expert tiles
+// alone do not, at least two 64-wide K blocks per split, at most 32 splits.
+int router_splits(int T, int H, int E, int num_sms) {
+  const int base = ((T + kRtBM - 1) / kRtBM) * ((E + kRtBN - 1) / kRtBN);
+  const int nkb = H / 64;
+  int s = base > 0 ? num_sms / base : 1;
+  s = s < 1 ? 1 : s;
+  const int cap = nkb / 2 < 32 ? nkb / 2 : 32;
+  s = s > cap ? cap : s;
+  s = s < 1 ? 1 : s;
+  const int kps = (nkb + s - 1) / s;
+  return (nkb + kps - 1) / kps;  // every split non-empty
+}
+}  // namespace
+
+size_t msv_router_workspace_size(int T, int H, int E) {
+  if (T < 0 || H <= 0 || H % 64 || E < 16 || E % 16 || E > 1024) return 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int nsm = 148;
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  // the splits' partial sums, then the summed logits
+  return ((size_t)router_splits(T, H, E, nsm) + 1) * (size_t)(T > 0 ? T : 1) * (size_t)E * sizeof(float) + 512;
+}
+
+int msv_router_from_hidden(const void* hidden, const void* gate_w, int T, int H, int E, int k, int renormalize,
+                           int round_logits_bf16, void* topk_w, int w_dtype, void* topk_ids, int ids_dtype,
+                           float* logits_out, void* workspace, size_t workspace_bytes, msv_stream_t stream) {
+  if (!hidden || !gate_w || !topk_ids || T < 0 || H <= 0 || H % 64 || E < 16 || E % 16 || E > 1024 || k < 1 ||
+      k > 16 || k > E)
+    return fail(MSV_ERR_INVALID,
+                "msv_router_from_hidden: bad arguments (T=%d H=%d E=%d k=%d; H %% 64 == 0, 16 <= E <= 1024, E %% 16 == 0)",
+                T, H, E, k);
+  if ((w_dtype != MSV_F32 && w_dtype != MSV_BF16) || (ids_dtype != MSV_I32 && ids_dtype != MSV_I64))
+    return fail(MSV_ERR_INVALID, "msv_router_from_hidden: dtype codes");
+  if (logits_out && !is_pow2_aligned(logits_out, 16))
+    return fail(MSV_ERR_INVALID, "msv_router_from_hidden: logits_out must be 16-byte aligned");
+  if (T == 0) return MSV_OK;
+  DeviceInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int nsplit = router_splits(T, H, E, d->num_sms);
+  const size_t part_bytes = (((size_t)nsplit * T * E * sizeof(float)) + 255) & ~(size_t)255;
+  const size_t need = part_bytes + (size_t)T * E * sizeof(float);
+  if (!workspace || workspace_bytes < need || !is_pow2_aligned(workspace, 256))
+    return fail(MSV_ERR_INVALID, "msv_router_from_hidden: workspace %zu < %zu bytes or not 256-byte aligned",
+                workspace_bytes, need);
+  static bool configured[64] = {};
+  if (!configured[dev]) {
+    if (int rc = cuda_check(cudaFuncSetAttribute(k_router_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, kRtSmem),
+                            "cudaFuncSetAttribute(router_gemm)"))
+      return rc;
+    configured[dev] = true;
+  }
+  RouterArgs a{};
+  if (int rc = tensor_map_bf16(&a.tmA, hidden, (uint64_t)T, (uint64_t)H, (uint64_t)H * 2, kRtBM)) return rc;
+  if (int rc = tensor_map_bf16(&a.tmB, gate_w, (uint64_t)E, (uint64_t)H, (uint64_t)H * 2, kRtBN)) return rc;
+  a.T = T;
+  a.H = H;
+  a.E = E;
+  const int nkb = H / 64;
+  a.kb_per_split = (nkb + nsplit - 1) / nsplit;
+  float* logits = logits_out ? logits_out : static_cast<float*>(workspace);
+  // one split: the GEMM writes the (rounded) logits itself; several: partial sums, then a sum
+  a.round_bf16 = nsplit == 1 && round_logits_bf16;
+  a.part = nsplit == 1 ? logits : static_cast<float*>(workspace);
+  a.err = d->err_word;
+  const dim3 grid((T + kRtBM - 1) / kRtBM, (E + kRtBN - 1) / kRtBN, nsplit);
+  k_router_gemm<<<grid, 128, kRtSmem, stream>>>(a);
+  if (int rc = cuda_check(cudaGetLastError(), "launch router_gemm")) return rc;
+  if (nsplit > 1) {
+    // the splits summed in order (and rounded) into the logits the routing reads
+    if (!logits_out) logits = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + part_bytes);
+    const int64_t n4 = (int64_t)T * E / 4;
+    k_router_sum_splits<<<(unsigned)((n4 + 255) / 256), 256, 0, stream>>>(a.part, nsplit, n4, round_logits_bf16 ? 1 : 0,
+                                                                            logits);
+    if (int rc = cuda_check(cudaGetLastError(), "launch router_sum_splits")) return rc;
+  }
+  k_route_topk<<<(T + kRouteWarps - 1) / kRouteWarps, kRouteWarps * 32, route_smem_bytes(E), stream>>>(
+      logits, E, T, E, k, 1, renormalize, topk_w, w_dtype, topk_ids, ids_dtype, nullptr);
   return cuda_check(cudaGetLastError(), "launch route_topk");
 }
 

@@ -18,6 +18,14 @@ def moe_gate(hidden: torch.Tensor, gate_weight: torch.Tensor, top_k: int | None 
     """Routing scores and top-k (``moe_dispatch.py:8-24``): fp32 logits, softmax, top-k,
     renormalise.  Returns ``(topk_ids [T,k] int32, topk_weights [T,k] fp32)``."""
     k = top_k if top_k is not None else config.NUM_EXPERTS_PER_TOK
+    t, h = hidden.shape
+    e = gate_weight.shape[0]
+    if (hidden.dtype == torch.bfloat16 and gate_weight.dtype == torch.bfloat16 and h % 64 == 0 and e % 16 == 0
+            and 16 <= e <= 1024):
+        # bf16 products are exact in fp32, so the tensor-core GEMM with fp32 accumulation and no
+        # final rounding computes the reference's fp32 linear up to the order of the fp32 sum
+        w, ids = moe.router_from_hidden(hidden, gate_weight, k, round_logits_bf16=False, w_dtype=torch.float32)
+        return ids, w
     logits = F.linear(hidden.float(), gate_weight.float())
     w, ids = moe.route_topk(logits.contiguous(), k, renormalize=True, w_dtype=torch.float32, ids_dtype=torch.int32)
     return ids, w

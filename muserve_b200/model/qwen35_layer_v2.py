@@ -1,10 +1,12 @@
 """MoE half of the reference's active layer (``muserve/model/qwen35_layer_v2.py``) on sm_100a.
 
 ``moe_forward(hidden, weights)`` keeps the reference's signature and weights-dict contract
-(``:561``, ``loader.py:212-264``).  The router GEMM stays ``F.linear`` in bf16 (``:568``, a
-plain cuBLAS GEMM); everything after it runs in the library's six kernels (router top-k,
-dispatch, gather+quantise, gate_up GEMM with SwiGLU+requant epilogue, down GEMM, combine +
-shared expert).  With tensor parallelism the per-rank partial ``[T,H]`` is all-reduced once
+(``:561``, ``loader.py:212-264``).  The router (``:567-572``) runs as the library's router GEMM
+on the tensor cores (bf16 x bf16 -> fp32, rounded to bf16 as ``bf16_linear(...).float()``) plus
+softmax / top-k; shapes that GEMM does not take (H % 64, E % 16) use ``F.linear`` and the
+library's top-k.  Everything after it runs in the library's layer kernels (dispatch,
+gather+quantise, gate_up GEMM with SwiGLU+requant epilogue, down GEMM, combine + shared
+expert).  With tensor parallelism the per-rank partial ``[T,H]`` is all-reduced once
 (the V1 / BASELINE placement, ``qwen35_layer.py:565-571``) instead of V2's ``[T*k,H]``
 buffer (``:652-657``); results differ from V2 only by bf16 rounding of partial sums.
 """
@@ -63,12 +65,16 @@ def moe_forward(hidden: torch.Tensor, weights: dict, *, top_k: int | None = None
     gate_w = weights["moe.gate.weight"]
     num_experts = gate_w.shape[0]
     tp, rank = get_tp_size(), get_tp_rank()
-    logits = bf16_linear(hidden, gate_w).float()                               # :568
+    hidden = hidden.contiguous()
     lay = _layout(weights, num_experts, tp)
     placement = 1 if (tp > 1 and lay == "expert") else 0
-    res = moe.moe_layer(hidden.contiguous(), weights, top_k=k, num_experts=num_experts, router_logits=logits,
-                        placement=placement, tp=tp, rank=rank,
-                        add_shared=(placement == 0 or rank == 0), return_routing=return_routing)
+    if hidden.shape[1] % 64 == 0 and num_experts % 16 == 0 and 16 <= num_experts <= 1024:
+        topk_w, topk_ids = moe.router_from_hidden(hidden, gate_w, k)               # :567-572
+        route = dict(topk_w=topk_w, topk_ids=topk_ids)
+    else:
+        route = dict(router_logits=bf16_linear(hidden, gate_w).float())            # :568
+    res = moe.moe_layer(hidden, weights, top_k=k, num_experts=num_experts, placement=placement, tp=tp,
+                        rank=rank, add_shared=(placement == 0 or rank == 0), return_routing=return_routing, **route)
     out = res[0] if return_routing else res
     if tp > 1:
         all_reduce(out)

@@ -35,6 +35,35 @@ def route_topk(logits: torch.Tensor, k: int, renormalize: bool = True,
     return w, ids
 
 
+def router_from_hidden(hidden: torch.Tensor, gate_weight: torch.Tensor, k: int, renormalize: bool = True,
+                       round_logits_bf16: bool = True, w_dtype: torch.dtype = torch.bfloat16,
+                       ids_dtype: torch.dtype = torch.int32, return_logits: bool = False):
+    """Router from the hidden states on the tensor cores: ``hidden @ gate_weight.T`` (bf16 in, fp32
+    accumulation), optionally rounded to bf16 (``qwen35_layer_v2.py:567-568``), then softmax,
+    top-k and renormalisation as :func:`route_topk` (``:569-572``).  With
+    ``round_logits_bf16=False`` and fp32 weights it is ``moe_dispatch.moe_gate``
+    (``kernels/moe_dispatch.py:8-24``).  Returns ``(topk_w, topk_ids[, logits])``."""
+    lib = _lib.load()
+    _cuda(hidden, "hidden")
+    _cuda(gate_weight, "gate_weight")
+    assert hidden.dtype == torch.bfloat16 and gate_weight.dtype == torch.bfloat16
+    hidden, gate_weight = hidden.contiguous(), gate_weight.contiguous()
+    t, h = hidden.shape
+    e, h2 = gate_weight.shape
+    assert h == h2
+    w = torch.empty(t, k, dtype=w_dtype, device=hidden.device)
+    ids = torch.empty(t, k, dtype=ids_dtype, device=hidden.device)
+    logits = torch.empty(t, e, dtype=torch.float32, device=hidden.device) if return_logits else None
+    nbytes = lib.msv_router_workspace_size(t, h, e)
+    if nbytes == 0:
+        check(_lib.MSV_ERR_INVALID, "msv_router_workspace_size")
+    ws = _lib.workspace(nbytes, hidden.device)
+    check(lib.msv_router_from_hidden(ptr(hidden), ptr(gate_weight), t, h, e, k, int(renormalize),
+                                     int(round_logits_bf16), ptr(w), _DT[w_dtype], ptr(ids), _DT[ids_dtype],
+                                     ptr(logits), ptr(ws), ws.numel(), stream_ptr()), "msv_router_from_hidden")
+    return (w, ids, logits) if return_logits else (w, ids)
+
+
 def topk_select(values: torch.Tensor, k: int, ids_dtype: torch.dtype = torch.int64):
     """``torch.topk(values, k)`` with torch's CPU tie order, on the GPU."""
     lib = _lib.load()
