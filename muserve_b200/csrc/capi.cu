@@ -245,6 +245,7 @@ int tensor_map_f32(CUtensorMap* out, const void* base, uint64_t rows, uint64_t c
 
 using G1Small = GemmCfg<32, 2, 1, 1>;   // gate+up -> SwiGLU -> e4m3, <= 32 rows per chunk
 using G2Small = GemmCfg<32, 1, 0, 1>;   // plain -> bf16, <= 32 rows per chunk
+using G2Pair = GemmCfg<32, 2, 0, 1>;    // plain -> bf16, two 128-row blocks per tile (32 KB of weights per stage)
 using G2Large = GemmCfg<192, 1, 0, 3>;  // plain -> bf16, <= 192 rows per chunk
 using R1 = RowsCfg<1, 32, 2>;          // tokens on M: gate+up halves -> SwiGLU -> e4m3 (K <= 4096)
 using R2 = RowsCfg<0, 8, 4>;           // tokens on M: plain -> bf16 (K <= 1024)
@@ -692,7 +693,7 @@ int msv_gemm_fp8_nt_groupwise(const uint8_t* a, const float* a_scale, int M, int
 namespace {
 struct LayerPlan {
   int T, H, E, k, I, Is, P, rows, e_local;
-  bool shared, small1, small2, rows1, rows2, gather;
+  bool shared, small1, small2, rows1, rows2, gather, pair2;
   int bn1, bn2, nb1, nb2, srows;
   size_t cap1, cap2;
 };
@@ -728,8 +729,11 @@ int plan_layer(const msv_moe_shape* s, LayerPlan* L) {
   L->rows2 = !L->small2 && (L->I / 128) % 4 == 0 && L->I / 128 <= R2::MAXKB;
   L->bn1 = L->rows1 ? R1::BM : G1Small::BN;
   L->bn2 = L->rows2 ? R2::BM : (L->small2 ? G2Small::BN : G2Large::BN);
+  // small-batch down GEMM: two 128-row blocks of H per tile, so each pipeline stage carries as
+  // many weight bytes as the gate_up GEMM's (gate + up)
+  L->pair2 = !L->rows2 && L->small2 && L->H % 256 == 0;
   L->nb1 = L->I / 128;
-  L->nb2 = L->H / 128;
+  L->nb2 = L->pair2 ? L->H / 256 : L->H / 128;
   L->srows = (L->rows + 3) & ~3;  // K-block stride of the activation scales (16-byte rows)
   // large batches quantise each token once and gather the e4m3 rows (16-byte scale rows)
   L->gather = L->P > kPermSingleMax && (L->H / 128) % 4 == 0;
@@ -1058,7 +1062,11 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
     g2.out = w.down;
     g2.out_ld = L.H;
     g2.err = d->err_word;
-    if (int rc = launch_gemm_variant(L.small2, g2, stream, d->num_sms)) return rc;
+    if (L.pair2) {
+      if (int rc = launch_gemm<G2Pair>(g2, stream, d->num_sms)) return rc;
+    } else {
+      if (int rc = launch_gemm_variant(L.small2, g2, stream, d->num_sms)) return rc;
+    }
   }
   if (int rc = mark(5)) return rc;
   // 6. weighted combine (+ shared expert)

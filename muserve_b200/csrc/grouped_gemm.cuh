@@ -185,8 +185,14 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
       const int4 td = args.tiles[tile];
       const int set = td.z >> 24, e = td.z & 0xFFFFFF;
       const int nr = td.y;
-      const int arow = e * args.a_expert_rows[set] + td.w * 128;
-      const float* wsp = args.ws[set][lane < NACC ? lane : 0] + e * args.ws_expert_stride[set] + td.w * args.ws_nb_stride;
+      // EPI 0 with NACC accumulators: a tile covers NACC consecutive 128-row weight blocks of one
+      // matrix (accumulator a: rows + 128 a, scale row + a); EPI 1: one block of gate and of up
+      constexpr int NBLK = C::EPI == 0 ? NACC : 1;
+      const int arow = e * args.a_expert_rows[set] + td.w * 128 * NBLK;
+      const int acc_l = lane < NACC ? lane : 0;
+      const float* wsp = C::EPI == 0
+                             ? args.ws[set][0] + e * args.ws_expert_stride[set] + (td.w * NBLK + acc_l) * args.ws_nb_stride
+                             : args.ws[set][acc_l] + e * args.ws_expert_stride[set] + td.w * args.ws_nb_stride;
       const float* asp = args.as + (int64_t)td.x * args.as_row;
       for (int kb = 0; kb < nkb; ++kb) {
         if (!mbar_wait(&empty[st.i], st.ph ^ 1, s_abort) || !mbar_wait(&sfree[sl.i], sl.ph ^ 1, s_abort)) {
@@ -197,7 +203,9 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
           uint8_t* sp = smem + st.i * C::STAGE_BYTES;
           mbar_arrive_expect_tx(&full[st.i], C::STAGE_BYTES);
 #pragma unroll
-          for (int a = 0; a < NACC; ++a) tma_load_2d(sp + a * C::A_BYTES, &args.tmA[set][a], &full[st.i], kb * 128, arow);
+          for (int a = 0; a < NACC; ++a)
+            tma_load_2d(sp + a * C::A_BYTES, &args.tmA[set][C::EPI == 0 ? 0 : a], &full[st.i], kb * 128,
+                        arow + (C::EPI == 0 ? a * 128 : 0));
           tma_load_2d(sp + NACC * C::A_BYTES, &args.tmB, &full[st.i], kb * 128, td.x);
         }
         float* slot = raw + sl.i * C::RAW_FLOATS;
@@ -368,10 +376,14 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
       if constexpr (C::EPI == 0) {
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
 #pragma unroll
-        for (int c = 0; c < CW; ++c) {
-          const int t = wg * CW + c;
-          if (t >= nr) break;
-          out[(row0 + t) * args.out_ld + ncol] = __float2bfloat16_rn(acc[0][c]);
+        for (int a = 0; a < NACC; ++a) {
+          const int col = (td.w * NACC + a) * 128 + lrow;
+#pragma unroll
+          for (int c = 0; c < CW; ++c) {
+            const int t = wg * CW + c;
+            if (t >= nr) break;
+            out[(row0 + t) * args.out_ld + col] = __float2bfloat16_rn(acc[a][c]);
+          }
         }
       } else {
         // SwiGLU exactly as the reference rounds it: gate/up GEMM outputs are bf16
