@@ -196,6 +196,70 @@ MSV_DEVICE int warp_partition(Arr a, int lo, int hi, float p, uint16_t* lpos, ui
   return cut;
 }
 
+// Fast path: when the k+1 largest values of the row (the k largest when k == n) are all
+// distinct, torch's result is unique, the k largest in descending order, whatever the
+// algorithm's internal order.  For rows of up to 512 values a warp holds the row in registers
+// (16 per lane) and selects in k+1 argmax rounds, stopping at the first tie; it writes the
+// result to positions [0,k) and returns true, or returns false with the row untouched (the
+// replay below then decides the order of the tied values).  Rows holding a NaN never come here.
+constexpr int kFastTopkMax = 512;
+__device__ __noinline__ bool warp_topk_distinct(Arr a, int n, int k) {
+  if (n > kFastTopkMax) return false;
+  const int lane = threadIdx.x & 31;
+  const int rounds = k < n ? k + 1 : k;
+  constexpr int NV = kFastTopkMax / 32;
+  float x[NV];
+  uint32_t taken = 0;  // bit j: element lane + 32 j selected or absent
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = lane + 32 * j;
+    if (i < n) x[j] = a.v[i];
+    else {
+      x[j] = 0.f;
+      taken |= 1u << j;
+    }
+  }
+  float sel_v = 0.f, prev = 0.f;
+  int sel_i = 0;
+  for (int r = 0; r < rounds; ++r) {
+    float best = 0.f;
+    int bj = -1;
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+      if (!((taken >> j) & 1u) && (bj < 0 || x[j] > best)) {
+        best = x[j];
+        bj = j;
+      }
+    int bi = bj < 0 ? 0x7fffffff : lane + 32 * bj;
+    int have = bj >= 0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      const int oh = __shfl_xor_sync(0xffffffffu, have, o);
+      if (oh && (!have || ob > best || (ob == best && oi < bi))) {
+        best = ob;
+        bi = oi;
+        have = oh;
+      }
+    }
+    if (r > 0 && !(prev > best)) return false;  // a tie (warp-uniform: all lanes hold the same pair)
+    prev = best;
+    if (lane == (bi & 31)) taken |= 1u << (bi >> 5);
+    if (lane == r) {
+      sel_v = best;
+      sel_i = bi;
+    }
+  }
+  __syncwarp();
+  if (lane < k) {
+    a.v[lane] = sel_v;
+    a.ix[lane] = (uint16_t)sel_i;
+  }
+  __syncwarp();
+  return true;
+}
+
 // Full torch-CPU topk replay on one row held in shared memory.  On return positions
 // [0,k) hold the result in torch's order.
 MSV_DEVICE void warp_topk_torch_cpu(Arr a, int n, int k, uint16_t* lpos, uint16_t* rpos) {
@@ -258,15 +322,20 @@ __global__ void __launch_bounds__(kRouteWarps * 32) k_route_topk(const float* __
   const float* row = logits + (int64_t)t * ld;
   float mx = -INFINITY;
   bool any_nan = false;
+  uint32_t low_bits = 0;  // zero when every value of the row is a bf16 value
   for (int i = lane; i < E; i += 32) {
     float x = row[i];
     v[i] = x;
     ix[i] = (uint16_t)i;
     mx = fmaxf(mx, x);
     any_nan |= (x != x);
+    low_bits |= __float_as_uint(x) & 0xffffu;
   }
   mx = warp_max(mx);
   any_nan = __any_sync(0xffffffffu, any_nan);
+  // rows of bf16 logits (8-bit significands) usually hold ties among their largest values, so
+  // they go straight to the replay; other rows try the distinct-values fast path first
+  const bool bf16_row = !__any_sync(0xffffffffu, low_bits != 0);
   // torch's softmax turns a whole row into NaN when it holds a NaN or +inf logit; select on
   // that all-NaN row then, exactly as torch.topk sees it.
   const bool all_nan = softmax && (any_nan || mx == INFINITY);
@@ -279,7 +348,7 @@ __global__ void __launch_bounds__(kRouteWarps * 32) k_route_topk(const float* __
     for (int i = lane; i < E; i += 32) v[i] = __int_as_float(0x7fffffff);
   __syncwarp();
   Arr a{v, ix};
-  warp_topk_torch_cpu(a, E, k, lpos, rpos);
+  if (any_nan || all_nan || bf16_row || !warp_topk_distinct(a, E, k)) warp_topk_torch_cpu(a, E, k, lpos, rpos);
   // weights: score_j = exp(x_j - max) * (1/sum); optional renormalisation over the k
   float s = 0.f;
   uint16_t id = 0;
