@@ -358,7 +358,7 @@ def run_ours(args, world, rank, local):
         "cpu_baseline": cpu,
     }
     if rank == 0:
-        print(json.dumps(res), flush=True)
+        emit(res)
 
 
 def cpu_baseline(x, logits, w, tokens):
@@ -431,7 +431,7 @@ def run_reference(args, world, rank):
     value = per_step * args.steps / dt
     sample = (f"{per_step} of {tokens} tokens per step (cycling), whole layer on one host (no TP split), "
               f"torch CPU, {os.cpu_count()} threads")
-    print(json.dumps({
+    emit(({
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "e4m3 dequantised to fp32 (torch CPU)",
@@ -440,7 +440,30 @@ def run_reference(args, world, rank):
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }), flush=True)
+    }))
+
+
+# The result line is the only thing this script writes to stdout: libraries that print there
+# (NCCL's version banner when NCCL_DEBUG asks for it, at communicator creation) write to
+# stderr instead, because fd 1 points at stderr while the script runs.
+_RESULT_FD = None
+
+
+def _claim_stdout() -> None:
+    global _RESULT_FD
+    if _RESULT_FD is None:
+        sys.stdout.flush()
+        _RESULT_FD = os.dup(1)
+        os.dup2(2, 1)
+
+
+def emit(obj: dict) -> None:
+    line = (json.dumps(obj) + "\n").encode()
+    if _RESULT_FD is None:
+        sys.stdout.write(line.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_RESULT_FD, line)
 
 
 def main():
@@ -457,6 +480,7 @@ def main():
     ap.add_argument("--clock-window-ms", type=float, default=500.0,
                     help="length of the clock-sampling window (0: timed region only, for profiler runs)")
     args = ap.parse_args()
+    _claim_stdout()
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))
