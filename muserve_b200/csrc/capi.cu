@@ -543,7 +543,7 @@ int msv_fp8_quant_128(const void* x, int64_t ldx, int M, int K, const int32_t* r
   a.scale = scale;
   a.s_row = s_row;
   a.s_kb = s_kb;
-  k_quant_rows<<<(M + kQuantWarps - 1) / kQuantWarps, kQuantWarps * 32, 0, stream>>>(a);
+  k_quant_rows<<<(M + kQuantRowsPerCta - 1) / kQuantRowsPerCta, kQuantWarps * 32, 0, stream>>>(a);
   return cuda_check(cudaGetLastError(), "launch quant");
 }
 
@@ -899,7 +899,7 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
     q.s_row = L.H / 128;
     q.s_kb = 1;
     if (!do_shared) q.gate_w = nullptr;
-    k_quant_rows<<<(L.T + kQuantWarps - 1) / kQuantWarps, kQuantWarps * 32, 0, stream>>>(q);
+    k_quant_rows<<<(L.T + kQuantRowsPerCta - 1) / kQuantRowsPerCta, kQuantWarps * 32, 0, stream>>>(q);
     if (int rc = cuda_check(cudaGetLastError(), "launch quant")) return rc;
     // ... then the routed (and shared-expert) rows copied into expert-sorted order
     GatherArgs g{};
@@ -926,7 +926,7 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
     q.scale = w.xs;
     q.s_row = 1;
     q.s_kb = L.srows;
-    k_quant_rows<<<(L.rows + kQuantWarps - 1) / kQuantWarps, kQuantWarps * 32, 0, stream>>>(q);
+    k_quant_rows<<<(L.rows + kQuantRowsPerCta - 1) / kQuantRowsPerCta, kQuantWarps * 32, 0, stream>>>(q);
     if (int rc = cuda_check(cudaGetLastError(), "launch quant")) return rc;
   }
   if (int rc = mark(3)) return rc;

@@ -27,76 +27,91 @@ struct QuantArgs {
   float* gate_val;
 };
 
-constexpr int kQuantWarps = 8;
+constexpr int kQuantWarps = 8;  // per CTA: kQuantWarps / kQuantSplit rows
+constexpr int kQuantSplit = 4;  // warps per row
+constexpr int kQuantRowsPerCta = kQuantWarps / kQuantSplit;
 
-// One warp per output row; each lane owns 8 consecutive channels (16 bytes) of a 256-channel
-// slab, so a 128-channel block is 16 lanes and its amax is a 4-step xor shuffle.
+// kQuantSplit warps per output row; warp p of a row takes the row's 256-channel slabs p,
+// p + kQuantSplit, ...  Each lane owns 8 consecutive channels (16 bytes) of a slab, so a
+// 128-channel block is 16 lanes of one warp and its amax is a 4-step xor shuffle.  The shared
+// gate's dot product is summed over the row's warps in warp order.
 __global__ void __launch_bounds__(kQuantWarps * 32) k_quant_rows(QuantArgs a) {
-  const int lane = threadIdx.x & 31;
-  const int r = blockIdx.x * kQuantWarps + (threadIdx.x >> 5);
-  if (r >= a.rows_a + a.rows_b) return;
-  int64_t src;
-  bool seg_b = r >= a.rows_a;
-  if (!seg_b) {
-    if (a.nvalid_a && r >= *a.nvalid_a) return;
-    src = a.idx_a ? a.idx_a[r] : r;
-    if (src < 0) return;
-  } else {
-    src = r - a.rows_a;
+  __shared__ float s_dot[kQuantWarps];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int part = warp % kQuantSplit;
+  const int r = blockIdx.x * (kQuantWarps / kQuantSplit) + warp / kQuantSplit;
+  bool active = r < a.rows_a + a.rows_b;
+  int64_t src = 0;
+  const bool seg_b = r >= a.rows_a;
+  if (active) {
+    if (!seg_b) {
+      if (a.nvalid_a && r >= *a.nvalid_a) active = false;
+      else src = a.idx_a ? a.idx_a[r] : r;
+      if (src < 0) active = false;
+    } else {
+      src = r - a.rows_a;
+    }
   }
-  const __nv_bfloat16* __restrict__ xr = a.x + src * a.ldx;
-  uint8_t* __restrict__ qr = a.q + (int64_t)r * a.ldq;
+  const bool want_gate = active && seg_b && a.gate_w != nullptr;
   float dot = 0.f;
-  const bool want_gate = seg_b && a.gate_w != nullptr;
-  constexpr int kBatch = 4;  // 256-channel slabs loaded before any is processed
-  for (int c0 = 0; c0 < a.K; c0 += 256 * kBatch) {
-    uint4 raw[kBatch];
+  if (active) {
+    const __nv_bfloat16* __restrict__ xr = a.x + src * a.ldx;
+    uint8_t* __restrict__ qr = a.q + (int64_t)r * a.ldq;
+    const int nslab = (a.K + 255) / 256;
+    constexpr int kBatch = 4;  // slabs loaded before any is processed
+    for (int s0 = part; s0 < nslab; s0 += kQuantSplit * kBatch) {
+      uint4 raw[kBatch];
 #pragma unroll
-    for (int b = 0; b < kBatch; ++b) {
-      const int c = c0 + b * 256 + lane * 8;
-      raw[b] = c < a.K ? *reinterpret_cast<const uint4*>(xr + c) : make_uint4(0, 0, 0, 0);
-    }
-#pragma unroll
-    for (int b = 0; b < kBatch; ++b) {
-      const int c = c0 + b * 256 + lane * 8;
-      float f[8];
-      const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw[b]);
-      float am = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        f[i] = __bfloat162float(h[i]);
-        am = nanmax(am, fabsf(f[i]));
-      }
-      if (want_gate && c < a.K) {
-        uint4 wraw = *reinterpret_cast<const uint4*>(a.gate_w + c);
-        const __nv_bfloat16* wh = reinterpret_cast<const __nv_bfloat16*>(&wraw);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) dot = fmaf(f[i], __bfloat162float(wh[i]), dot);
+      for (int b = 0; b < kBatch; ++b) {
+        const int c = (s0 + b * kQuantSplit) * 256 + lane * 8;
+        raw[b] = c < a.K ? *reinterpret_cast<const uint4*>(xr + c) : make_uint4(0, 0, 0, 0);
       }
 #pragma unroll
-      for (int o = 8; o > 0; o >>= 1) am = nanmax(am, __shfl_xor_sync(0xffffffffu, am, o));
-      // s = clamp(amax, min=1e-12) / 448 (NaN propagates as in torch.clamp)
-      const float s = (am != am) ? am : __fdiv_rn(fmaxf(am, 1e-12f), 448.0f);
-      if (c < a.K) {
-        uint32_t packed[2];
+      for (int b = 0; b < kBatch; ++b) {
+        const int c = (s0 + b * kQuantSplit) * 256 + lane * 8;
+        float f[8];
+        const uint32_t w4[4] = {raw[b].x, raw[b].y, raw[b].z, raw[b].w};
+        float am = 0.f;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float lo = clamp_pm(__fdiv_rn(f[2 * i], s), 448.0f);
-          float hi = clamp_pm(__fdiv_rn(f[2 * i + 1], s), 448.0f);
-          uint16_t pr = f32x2_to_e4m3x2(lo, hi);
-          if (i & 1) packed[i >> 1] |= (uint32_t)pr << 16;
-          else packed[i >> 1] = pr;
+        for (int i = 0; i < 8; ++i) {
+          f[i] = bf16_bits_to_f32(w4[i >> 1], i & 1);
+          am = nanmax(am, fabsf(f[i]));
         }
-        *reinterpret_cast<uint2*>(qr + c) = make_uint2(packed[0], packed[1]);
-        if ((lane & 15) == 0) a.scale[(int64_t)r * a.s_row + (int64_t)(c / 128) * a.s_kb] = s;
+        if (want_gate && c < a.K) {
+          const uint4 wraw = *reinterpret_cast<const uint4*>(a.gate_w + c);
+          const uint32_t g4[4] = {wraw.x, wraw.y, wraw.z, wraw.w};
+#pragma unroll
+          for (int i = 0; i < 8; ++i) dot = fmaf(f[i], bf16_bits_to_f32(g4[i >> 1], i & 1), dot);
+        }
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) am = nanmax(am, __shfl_xor_sync(0xffffffffu, am, o));
+        // s = clamp(amax, min=1e-12) / 448 (NaN propagates as in torch.clamp)
+        const float sc = (am != am) ? am : __fdiv_rn(fmaxf(am, 1e-12f), 448.0f);
+        if (c < a.K) {
+          uint32_t packed[2];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float lo = clamp_pm(__fdiv_rn(f[2 * i], sc), 448.0f);
+            const float hi = clamp_pm(__fdiv_rn(f[2 * i + 1], sc), 448.0f);
+            const uint16_t pr = f32x2_to_e4m3x2(lo, hi);
+            if (i & 1) packed[i >> 1] |= (uint32_t)pr << 16;
+            else packed[i >> 1] = pr;
+          }
+          *reinterpret_cast<uint2*>(qr + c) = make_uint2(packed[0], packed[1]);
+          if ((lane & 15) == 0) a.scale[(int64_t)r * a.s_row + (int64_t)(c / 128) * a.s_kb] = sc;
+        }
       }
     }
   }
-  if (want_gate) {
+  if (a.gate_w != nullptr) {  // uniform over the block
     dot = warp_sum(dot);
-    if (lane == 0) {
-      float lg = bf16_round(dot);
-      float sg = bf16_round(1.0f / (1.0f + expf(-lg)));
+    if (lane == 0) s_dot[warp] = dot;
+    __syncthreads();
+    if (want_gate && part == 0 && lane == 0) {
+      float d = s_dot[warp];
+      for (int p = 1; p < kQuantSplit; ++p) d += s_dot[warp + p];
+      const float lg = bf16_round(d);
+      const float sg = bf16_round(1.0f / (1.0f + expf(-lg)));
       a.gate_val[src] = sg;
     }
   }

@@ -323,6 +323,7 @@ __global__ void __launch_bounds__(kRouteWarps * 32) k_route_topk(const float* __
   float mx = -INFINITY;
   bool any_nan = false;
   uint32_t low_bits = 0;  // zero when every value of the row is a bf16 value
+#pragma unroll 8
   for (int i = lane; i < E; i += 32) {
     float x = row[i];
     v[i] = x;
