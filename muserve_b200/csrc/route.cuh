@@ -499,9 +499,11 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermuteArgs p) {
   int* offsets = counts + E;             // [E+1]
   int* scratch = offsets + E + 1;        // [E]
   const int P = p.T * p.k;
-  const int C = (P + kPermWarps - 1) / kPermWarps;
-  const int c0 = min(P, warp * C), c1 = min(P, c0 + C);
-  for (int i = threadIdx.x; i < kPermWarps * E; i += kPermThreads) hist[i] = 0;
+  // counting warps: at least 64 slots each, so small batches sum few per-warp histograms
+  const int HW = max(1, min(kPermWarps, (P + 63) / 64));
+  const int C = (P + HW - 1) / HW;
+  const int c0 = warp < HW ? min(P, warp * C) : P, c1 = warp < HW ? min(P, c0 + C) : P;
+  for (int i = threadIdx.x; i < HW * E; i += kPermThreads) hist[i] = 0;
   __syncthreads();
   int nloc = 0;
   for (int f = c0 + lane; f < c1; f += 32) {
@@ -519,7 +521,7 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermuteArgs p) {
   // per-expert totals
   for (int e = threadIdx.x; e < E; e += kPermThreads) {
     int c = 0;
-    for (int w = 0; w < kPermWarps; ++w) c += hist[w * E + e];
+    for (int w = 0; w < HW; ++w) c += hist[w * E + e];
     counts[e] = c;
   }
   __syncthreads();
@@ -536,7 +538,7 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermuteArgs p) {
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += kPermThreads) {
     int run = offsets[e];
-    for (int w = 0; w < kPermWarps; ++w) {
+    for (int w = 0; w < HW; ++w) {
       int c = hist[w * E + e];
       hist[w * E + e] = run;
       run += c;
