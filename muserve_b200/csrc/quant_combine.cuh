@@ -202,7 +202,7 @@ struct CombineArgs {
 };
 
 constexpr int kCombineThreads = 512;  // most threads a CTA is launched with
-constexpr int kCombineBatch = 12;  // slot rows loaded before any is summed (top-10 in one round)
+constexpr int kCombineBatch = 8;  // slot rows loaded before any is summed
 
 inline int combine_threads(int H) {
   const int t = ((H / 8 + 31) / 32) * 32;
@@ -211,9 +211,10 @@ inline int combine_threads(int H) {
 
 // One CTA per token; each thread produces 8 consecutive channels per pass (one pass when
 // H <= 4096).  Warp 0 reads the token's k slots in parallel (and orders them by expert id for
-// the per-expert modes); the channel loop loads 12 slot rows before it sums them.
+// the per-expert modes); the channel loop loads 8 slot rows before it sums them (two CTAs
+// per SM keep enough rows in flight at large batches).
 template <int MODE>
-__global__ void __launch_bounds__(kCombineThreads, 1) k_combine(CombineArgs a) {
+__global__ void __launch_bounds__(kCombineThreads, 2) k_combine(CombineArgs a) {
   const int t = blockIdx.x;
   __shared__ int s_row[16];
   __shared__ float s_w[16];
