@@ -210,11 +210,22 @@ def run_ours(args, world, rank, local):
     for row in evs:  # create the event handles before anything is timed
         for e in row:
             e.record(stream)
-    ev_arrays = [(ctypes.c_void_p * nst)(*[e.cuda_event for e in row]) for row in evs]
+    # Timed steps record only the events around the two GEMMs (indices 3, 4, 5: each recorded
+    # event between kernels costs about 3 us of device time); the other stages are timed in
+    # separate fully instrumented steps after the timed region.
+    GEMM_EV = (3, 4, 5)
+    ev_arrays = [(ctypes.c_void_p * nst)(*[e.cuda_event if j in GEMM_EV else None for j, e in enumerate(row)])
+                 for row in evs]
+    n_prof = min(args.steps, 10)
+    evs_p = [[torch.cuda.Event(enable_timing=True) for _ in range(nst)] for _ in range(n_prof)]
+    for row in evs_p:
+        for e in row:
+            e.record(stream)
+    ev_arrays_p = [(ctypes.c_void_p * nst)(*[e.cuda_event for e in row]) for row in evs_p]
 
-    def step(i=None):
+    def step(i=None, prof=False):
         if i is not None:
-            arr = ev_arrays[i]
+            arr = ev_arrays_p[i] if prof else ev_arrays[i]
             rc = lib.msv_moe_forward_profiled(ctypes.byref(shape), ctypes.byref(ws_struct), x.data_ptr(),
                                               logits.data_ptr(), tw.data_ptr(), tid.data_ptr(), out.data_ptr(), 0,
                                               wsbuf.data_ptr(), nbytes, sp, arr)
@@ -223,10 +234,10 @@ def run_ours(args, world, rank, local):
                                      tw.data_ptr(), tid.data_ptr(), out.data_ptr(), 0, wsbuf.data_ptr(), nbytes, sp)
         _lib.check(rc, "msv_moe_forward")
         if tp > 1:
-            if i is not None:
+            if i is not None and not prof:
                 ar_ev[i][0].record(stream)
             dist.all_reduce(out)
-            if i is not None:
+            if i is not None and not prof:
                 ar_ev[i][1].record(stream)
 
     for _ in range(args.warmup):
@@ -266,8 +277,16 @@ def run_ours(args, world, rank, local):
     barrier()
     ms_total = max_over_ranks(t0.elapsed_time(t1))
     _lib.check(lib.msv_check_device_error(sp), "timed region")
-    stage_ms = {s: statistics.mean(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(args.steps))
+    # the small stages from fully instrumented steps after the timed region (same collectives on
+    # every rank), the GEMMs from the timed steps themselves
+    for i in range(n_prof):
+        step(i, prof=True)
+    torch.cuda.synchronize()
+    stage_ms = {s: statistics.mean(evs_p[i][j].elapsed_time(evs_p[i][j + 1]) for i in range(n_prof))
                 for j, s in enumerate(STAGES)}
+    for j, s in enumerate(STAGES):
+        if j in GEMM_EV and j + 1 in GEMM_EV:
+            stage_ms[s] = statistics.mean(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(args.steps))
     ar_ms = statistics.mean(a.elapsed_time(b) for a, b in ar_ev) if tp > 1 else 0.0
     ms_step = ms_total / args.steps
     value = tokens * args.steps / (ms_total / 1e3)

@@ -224,6 +224,7 @@ int msv_moe_forward(const msv_moe_shape* shape, const msv_moe_weights* weights, 
  * msv_moe_forward that also records 7 CUDA events on `stream` (events: cudaEvent_t[7]): before
  * the router, the dispatch, the gather+quantise, the gate_up GEMM, the down GEMM and the
  * combine, and after the combine, so a caller can time each kernel on the launching stream.
+ * NULL entries are skipped (each recorded event costs some device time between kernels).
  * Same work and results as msv_moe_forward (no reference counterpart: profiling hook).
  */
 int msv_moe_forward_profiled(const msv_moe_shape* shape, const msv_moe_weights* weights, const void* hidden,

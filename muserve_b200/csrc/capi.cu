@@ -794,7 +794,7 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
                      void* topk_w, int32_t* topk_ids, void* out, int flags, void* workspace, size_t ws_bytes,
                      cudaStream_t stream, cudaEvent_t* ev) {
   auto mark = [&](int i) -> int {
-    return ev ? cuda_check(cudaEventRecord(ev[i], stream), "cudaEventRecord") : (int)MSV_OK;
+    return (ev && ev[i]) ? cuda_check(cudaEventRecord(ev[i], stream), "cudaEventRecord") : (int)MSV_OK;
   };
   LayerPlan L;
   if (int rc = plan_layer(s, &L)) return rc;
