@@ -262,7 +262,7 @@ int launch_gemm(const GemmArgs& a, cudaStream_t st, int num_sms) {
       return rc;
     configured[dev] = true;
   }
-  k_grouped_gemm<C><<<num_sms, C::THREADS, C::SMEM_BYTES, st>>>(a);
+  launch_k(k_grouped_gemm<C>, dim3(num_sms), dim3(C::THREADS), C::SMEM_BYTES, st, a);
   return cuda_check(cudaGetLastError(), "launch grouped_gemm");
 }
 
@@ -278,7 +278,7 @@ int launch_gemm_rows(const RowsArgs& a, cudaStream_t st, int num_sms) {
       return rc;
     configured[dev] = true;
   }
-  k_grouped_gemm_rows<C><<<num_sms, C::THREADS, C::SMEM_BYTES, st>>>(a);
+  launch_k(k_grouped_gemm_rows<C>, dim3(num_sms), dim3(C::THREADS), C::SMEM_BYTES, st, a);
   return cuda_check(cudaGetLastError(), "launch grouped_gemm_rows");
 }
 
@@ -391,7 +391,7 @@ int msv_route_topk(const float* logits, int64_t ld, int T, int E, int k, int ren
     return fail(MSV_ERR_INVALID, "msv_route_topk: dtype codes");
   if (T == 0) return MSV_OK;
   const size_t sm = route_smem_bytes(E);
-  k_route_topk<<<(T + kRouteWarps - 1) / kRouteWarps, kRouteWarps * 32, sm, stream>>>(
+  launch_k(k_route_topk, dim3((T + kRouteWarps - 1) / kRouteWarps), dim3(kRouteWarps * 32), sm, stream, 
       logits, ld, T, E, k, 1, renormalize, topk_w, w_dtype, topk_ids, ids_dtype, nullptr);
   return cuda_check(cudaGetLastError(), "launch route_topk");
 }
@@ -466,17 +466,17 @@ int msv_router_from_hidden(const void* hidden, const void* gate_w, int T, int H,
   a.part = nsplit == 1 ? logits : static_cast<float*>(workspace);
   a.err = d->err_word;
   const dim3 grid((T + kRtBM - 1) / kRtBM, (E + kRtBN - 1) / kRtBN, nsplit);
-  k_router_gemm<<<grid, 128, kRtSmem, stream>>>(a);
+  launch_k(k_router_gemm, dim3(grid), dim3(128), kRtSmem, stream, a);
   if (int rc = cuda_check(cudaGetLastError(), "launch router_gemm")) return rc;
   if (nsplit > 1) {
     // the splits summed in order (and rounded) into the logits the routing reads
     if (!logits_out) logits = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + part_bytes);
     const int64_t n4 = (int64_t)T * E / 4;
-    k_router_sum_splits<<<(unsigned)((n4 + 255) / 256), 256, 0, stream>>>(a.part, nsplit, n4, round_logits_bf16 ? 1 : 0,
+    launch_k(k_router_sum_splits, dim3((unsigned)((n4 + 255) / 256)), dim3(256), 0, stream, a.part, nsplit, n4, round_logits_bf16 ? 1 : 0,
                                                                             logits);
     if (int rc = cuda_check(cudaGetLastError(), "launch router_sum_splits")) return rc;
   }
-  k_route_topk<<<(T + kRouteWarps - 1) / kRouteWarps, kRouteWarps * 32, route_smem_bytes(E), stream>>>(
+  launch_k(k_route_topk, dim3((T + kRouteWarps - 1) / kRouteWarps), dim3(kRouteWarps * 32), route_smem_bytes(E), stream, 
       logits, E, T, E, k, 1, renormalize, topk_w, w_dtype, topk_ids, ids_dtype, nullptr);
   return cuda_check(cudaGetLastError(), "launch route_topk");
 }
@@ -487,7 +487,7 @@ int msv_topk_select(const float* values, int64_t ld, int T, int E, int k, void* 
     return fail(MSV_ERR_INVALID, "msv_topk_select: bad arguments");
   if (ids_dtype != MSV_I32 && ids_dtype != MSV_I64) return fail(MSV_ERR_INVALID, "msv_topk_select: ids dtype");
   if (T == 0) return MSV_OK;
-  k_route_topk<<<(T + kRouteWarps - 1) / kRouteWarps, kRouteWarps * 32, route_smem_bytes(E), stream>>>(
+  launch_k(k_route_topk, dim3((T + kRouteWarps - 1) / kRouteWarps), dim3(kRouteWarps * 32), route_smem_bytes(E), stream, 
       values, ld, T, E, k, 0, 0, nullptr, MSV_F32, topk_ids, ids_dtype, out_values);
   return cuda_check(cudaGetLastError(), "launch topk_select");
 }
@@ -521,7 +521,7 @@ int msv_moe_permute(const void* topk_ids, int ids_dtype, int T, int k, int num_e
     if (int rc = cuda_check(cudaFuncSetAttribute(k_permute, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
                             "cudaFuncSetAttribute(permute)"))
       return rc;
-  k_permute<<<1, kPermThreads, sm, stream>>>(p);
+  launch_k(k_permute, dim3(1), dim3(kPermThreads), sm, stream, p);
   return cuda_check(cudaGetLastError(), "launch permute");
 }
 
@@ -543,7 +543,7 @@ int msv_fp8_quant_128(const void* x, int64_t ldx, int M, int K, const int32_t* r
   a.scale = scale;
   a.s_row = s_row;
   a.s_kb = s_kb;
-  k_quant_rows<<<(M + kQuantRowsPerCta - 1) / kQuantRowsPerCta, kQuantWarps * 32, 0, stream>>>(a);
+  launch_k(k_quant_rows, dim3((M + kQuantRowsPerCta - 1) / kQuantRowsPerCta), dim3(kQuantWarps * 32), 0, stream, a);
   return cuda_check(cudaGetLastError(), "launch quant");
 }
 
@@ -571,7 +571,7 @@ int msv_ragged_moe_gemm_fp8(const uint8_t* a, const float* a_scale, int M, int K
   Carver c{static_cast<uint8_t*>(workspace)};
   int4* tiles = c.take<int4>(cap);
   int* ntiles = c.take<int>(1);
-  k_tiles_from_runs<<<1, 1024, 0, stream>>>(m_indices, M, bn, nb, tiles, ntiles, (int)cap);
+  launch_k(k_tiles_from_runs, dim3(1), dim3(1024), 0, stream, m_indices, M, bn, nb, tiles, ntiles, (int)cap);
   if (int rc = cuda_check(cudaGetLastError(), "launch tiles_from_runs")) return rc;
   GemmArgs g{};
   if (int rc = tensor_map(&g.tmA[0][0], w, (uint64_t)E * N, K, K, 128)) return rc;
@@ -621,7 +621,7 @@ int msv_ragged_moe_gemm_fp8_noalloc(const uint8_t* a, const float* a_scale, int 
   const int bn = variant_bn(small), nb = N / 128;
   int* ntiles = reinterpret_cast<int*>(scratch);
   int4* tiles = reinterpret_cast<int4*>(scratch + kNoAllocTileOffset);
-  k_tiles_from_runs<<<1, 1024, 0, stream>>>(m_indices, M, bn, nb, tiles, ntiles, (int)need);
+  launch_k(k_tiles_from_runs, dim3(1), dim3(1024), 0, stream, m_indices, M, bn, nb, tiles, ntiles, (int)need);
   if (int rc = cuda_check(cudaGetLastError(), "launch tiles_from_runs")) return rc;
   GemmArgs g{};
   if (int rc = tensor_map_uncached(&g.tmA[0][0], w, (uint64_t)E * N, K, K, 128)) return rc;
@@ -666,7 +666,7 @@ int msv_gemm_fp8_nt_groupwise(const uint8_t* a, const float* a_scale, int M, int
   Carver c{static_cast<uint8_t*>(workspace)};
   int4* tiles = c.take<int4>(tile_cap(1, M, 32, nb));
   int* ntiles = c.take<int>(1);
-  k_tiles_dense<<<64, 256, 0, stream>>>(M, bn, nb, tiles, ntiles);
+  launch_k(k_tiles_dense, dim3(64), dim3(256), 0, stream, M, bn, nb, tiles, ntiles);
   if (int rc = cuda_check(cudaGetLastError(), "launch tiles_dense")) return rc;
   GemmArgs g{};
   if (int rc = tensor_map(&g.tmA[0][0], b, N, K, K, 128)) return rc;
@@ -825,7 +825,7 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
   void* rw = topk_w ? topk_w : w.w;
   if (int rc = mark(0)) return rc;
   if (!given) {
-    k_route_topk<<<(L.T + kRouteWarps - 1) / kRouteWarps, kRouteWarps * 32, route_smem_bytes(L.E), stream>>>(
+    launch_k(k_route_topk, dim3((L.T + kRouteWarps - 1) / kRouteWarps), dim3(kRouteWarps * 32), route_smem_bytes(L.E), stream, 
         logits, L.E, L.T, L.E, L.k, 1, 1, rw, s->weights_dtype, ids, MSV_I32, nullptr);
     if (int rc = cuda_check(cudaGetLastError(), "launch route_topk")) return rc;
   }
@@ -864,7 +864,7 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
       if (int rc = cuda_check(cudaFuncSetAttribute(k_permute, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psm),
                               "cudaFuncSetAttribute(permute)"))
         return rc;
-    k_permute<<<1, kPermThreads, psm, stream>>>(p);
+    launch_k(k_permute, dim3(1), dim3(kPermThreads), psm, stream, p);
     if (int rc = cuda_check(cudaGetLastError(), "launch permute")) return rc;
   } else {
     // the same sort over blocks of slots: counts, one scan block (+ tile lists), scatter
@@ -874,11 +874,11 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
       if (int rc = cuda_check(cudaFuncSetAttribute(k_perm_count, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csm),
                               "cudaFuncSetAttribute(perm_count)"))
         return rc;
-    k_perm_count<<<ps.nblk, kPermThreads, csm, stream>>>(p, ps);
+    launch_k(k_perm_count, dim3(ps.nblk), dim3(kPermThreads), csm, stream, p, ps);
     if (int rc = cuda_check(cudaGetLastError(), "launch perm_count")) return rc;
-    k_perm_scan<<<1, kPermThreads, perm_scan_smem_bytes(L.e_local), stream>>>(p, ps);
+    launch_k(k_perm_scan, dim3(1), dim3(kPermThreads), perm_scan_smem_bytes(L.e_local), stream, p, ps);
     if (int rc = cuda_check(cudaGetLastError(), "launch perm_scan")) return rc;
-    k_perm_scatter<<<(L.P + 255) / 256, 256, 0, stream>>>(p, ps);
+    launch_k(k_perm_scatter, dim3((L.P + 255) / 256), dim3(256), 0, stream, p, ps);
     if (int rc = cuda_check(cudaGetLastError(), "launch perm_scatter")) return rc;
   }
   if (int rc = mark(2)) return rc;
@@ -899,7 +899,7 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
     q.s_row = L.H / 128;
     q.s_kb = 1;
     if (!do_shared) q.gate_w = nullptr;
-    k_quant_rows<<<(L.T + kQuantRowsPerCta - 1) / kQuantRowsPerCta, kQuantWarps * 32, 0, stream>>>(q);
+    launch_k(k_quant_rows, dim3((L.T + kQuantRowsPerCta - 1) / kQuantRowsPerCta), dim3(kQuantWarps * 32), 0, stream, q);
     if (int rc = cuda_check(cudaGetLastError(), "launch quant")) return rc;
     // ... then the routed (and shared-expert) rows copied into expert-sorted order
     GatherArgs g{};
@@ -914,7 +914,7 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
     g.scale = w.xs;
     g.s_kb = L.srows;
     const int gwarps = (L.rows + 31) / 32;
-    k_gather_rows<<<(gwarps + kGatherWarps - 1) / kGatherWarps, kGatherWarps * 32, 0, stream>>>(g);
+    launch_k(k_gather_rows, dim3((gwarps + kGatherWarps - 1) / kGatherWarps), dim3(kGatherWarps * 32), 0, stream, g);
     if (int rc = cuda_check(cudaGetLastError(), "launch gather")) return rc;
   } else {
     q.rows_a = L.P;
@@ -926,7 +926,7 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
     q.scale = w.xs;
     q.s_row = 1;
     q.s_kb = L.srows;
-    k_quant_rows<<<(L.rows + kQuantRowsPerCta - 1) / kQuantRowsPerCta, kQuantWarps * 32, 0, stream>>>(q);
+    launch_k(k_quant_rows, dim3((L.rows + kQuantRowsPerCta - 1) / kQuantRowsPerCta), dim3(kQuantWarps * 32), 0, stream, q);
     if (int rc = cuda_check(cudaGetLastError(), "launch quant")) return rc;
   }
   if (int rc = mark(3)) return rc;

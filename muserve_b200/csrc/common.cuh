@@ -20,6 +20,31 @@ __device__ __forceinline__ float bf16_bits_to_f32(uint32_t w, int hi) {
   return __uint_as_float(hi ? (w & 0xffff0000u) : (w << 16));
 }
 
+// Programmatic dependent launch.  Every kernel of this library is launched (launch_k) so that it
+// may start while the previous kernel on its stream is finishing.  pdl_wait() blocks until that
+// kernel has completed and its writes are visible; each kernel calls it before touching any
+// global memory another kernel of the stream reads or writes (only its own set-up of shared
+// memory, barriers and TMEM comes first).  pdl_trigger() lets the next kernel start launching;
+// kernels call it once their main work is done.
+MSV_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+MSV_DEVICE void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                            Args&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // Every device-side wait gives up after this long and reports MSV_ERR_TIMEOUT through the
 // kernel's error word; nothing in these kernels can spin forever.  Hot-path waits count SM
 // cycles (clock64, cheap to read); 4e9 cycles is about 2 s at the B200's 1.97 GHz.

@@ -172,6 +172,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
+  pdl_wait();
   const int ntiles = *args.num_tiles;
   const int nkb = args.num_kb;
 
@@ -424,6 +425,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
   if (threadIdx.x == 0 && *s_abort) atomicExch(args.err, (int)MSV_ERR_TIMEOUT);
+  pdl_trigger();
 }
 
 }  // namespace msv

@@ -130,6 +130,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm_rows(const __gri
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
+  pdl_wait();
   const int ntiles = *args.num_tiles;
 
   if (warp == 0) {
@@ -391,6 +392,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm_rows(const __gri
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
   if (threadIdx.x == 0 && *s_abort) atomicExch(args.err, (int)MSV_ERR_TIMEOUT);
+  pdl_trigger();
 }
 
 }  // namespace msv

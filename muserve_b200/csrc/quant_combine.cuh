@@ -36,6 +36,7 @@ constexpr int kQuantRowsPerCta = kQuantWarps / kQuantSplit;
 // 128-channel block is 16 lanes of one warp and its amax is a 4-step xor shuffle.  The shared
 // gate's dot product is summed over the row's warps in warp order.
 __global__ void __launch_bounds__(kQuantWarps * 32) k_quant_rows(QuantArgs a) {
+  pdl_wait();
   __shared__ float s_dot[kQuantWarps];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int part = warp % kQuantSplit;
@@ -115,6 +116,7 @@ __global__ void __launch_bounds__(kQuantWarps * 32) k_quant_rows(QuantArgs a) {
       a.gate_val[src] = sg;
     }
   }
+  pdl_trigger();
 }
 
 // Large batches quantise every token once (k_quant_rows over the T token rows, into a
@@ -140,6 +142,7 @@ constexpr int kGatherWarps = 8;
 // A warp moves 32 consecutive rows: each row's bytes with 16-byte lanes, then the 32 rows'
 // scales one K block at a time (lane = row, so each K block is one coalesced store).
 __global__ void __launch_bounds__(kGatherWarps * 32) k_gather_rows(GatherArgs a) {
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int r0 = (blockIdx.x * kGatherWarps + (threadIdx.x >> 5)) * 32;
   const int rows = a.rows_a + a.rows_b;
@@ -182,6 +185,7 @@ __global__ void __launch_bounds__(kGatherWarps * 32) k_gather_rows(GatherArgs a)
       a.scale[(int64_t)(kb + 3) * a.s_kb + rl] = v.w;
     }
   }
+  pdl_trigger();
 }
 
 struct CombineArgs {
@@ -215,6 +219,7 @@ inline int combine_threads(int H) {
 // per SM keep enough rows in flight at large batches).
 template <int MODE>
 __global__ void __launch_bounds__(kCombineThreads, 2) k_combine(CombineArgs a) {
+  pdl_wait();
   const int t = blockIdx.x;
   __shared__ int s_row[16];
   __shared__ float s_w[16];
@@ -294,13 +299,14 @@ __global__ void __launch_bounds__(kCombineThreads, 2) k_combine(CombineArgs a) {
     }
     *reinterpret_cast<uint4*>(a.out + (int64_t)t * a.ld_out + c) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
   }
+  pdl_trigger();
 }
 
 inline void launch_combine(const CombineArgs& a, cudaStream_t stream) {
   const dim3 grid(a.T), block(combine_threads(a.H));
-  if (a.mode == MSV_COMBINE_V2) k_combine<MSV_COMBINE_V2><<<grid, block, 0, stream>>>(a);
-  else if (a.mode == MSV_COMBINE_DISPATCH) k_combine<MSV_COMBINE_DISPATCH><<<grid, block, 0, stream>>>(a);
-  else k_combine<MSV_COMBINE_BATCHED><<<grid, block, 0, stream>>>(a);
+  if (a.mode == MSV_COMBINE_V2) launch_k(k_combine<MSV_COMBINE_V2>, dim3(grid), dim3(block), 0, stream, a);
+  else if (a.mode == MSV_COMBINE_DISPATCH) launch_k(k_combine<MSV_COMBINE_DISPATCH>, dim3(grid), dim3(block), 0, stream, a);
+  else launch_k(k_combine<MSV_COMBINE_BATCHED>, dim3(grid), dim3(block), 0, stream, a);
 }
 
 }  // namespace msv

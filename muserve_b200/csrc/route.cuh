@@ -310,6 +310,7 @@ __global__ void __launch_bounds__(kRouteWarps * 32) k_route_topk(const float* __
                                                                   void* __restrict__ out_w, int w_dtype,
                                                                   void* __restrict__ out_ids, int ids_dtype,
                                                                   float* __restrict__ out_vals) {
+  pdl_wait();
   extern __shared__ __align__(16) uint8_t sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * kRouteWarps + warp;
@@ -373,6 +374,7 @@ __global__ void __launch_bounds__(kRouteWarps * 32) k_route_topk(const float* __
     if (ids_dtype == MSV_I64) reinterpret_cast<int64_t*>(out_ids)[o] = id;
     else reinterpret_cast<int32_t*>(out_ids)[o] = id;
   }
+  pdl_trigger();
 }
 
 size_t route_smem_bytes(int E) {
@@ -489,6 +491,7 @@ MSV_DEVICE void build_tiles(const PermuteArgs& p, const int* counts, const int* 
 // walks the chunk in order and ranks equal experts inside each 32-slot batch with
 // __match_any_sync, which keeps the sort stable.
 __global__ void __launch_bounds__(kPermThreads) k_permute(PermuteArgs p) {
+  pdl_wait();
   extern __shared__ __align__(16) int hist[];  // [kPermWarps][e_local], then scratch
   __shared__ int s_nloc[kPermWarps];
   __shared__ int s_total;
@@ -582,6 +585,7 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermuteArgs p) {
   }
   if (p.tiles1) build_tiles(p, counts, offsets, scratch, s_warp, p.tiles1, p.ntiles1, p.bn1, p.nb1);
   if (p.tiles2) build_tiles(p, counts, offsets, scratch, s_warp, p.tiles2, p.ntiles2, p.bn2, p.nb2);
+  pdl_trigger();
 }
 
 size_t permute_smem_bytes(int e_local) { return (size_t)(kPermWarps * e_local + 3 * e_local + 1) * sizeof(int); }
@@ -607,6 +611,7 @@ struct PermuteScratch {
 size_t perm_count_smem_bytes(int e_local) { return (size_t)(kPermWarps * e_local) * sizeof(int); }
 
 __global__ void __launch_bounds__(kPermThreads) k_perm_count(PermuteArgs p, PermuteScratch s) {
+  pdl_wait();
   extern __shared__ __align__(16) int wc[];  // [kPermWarps][e_local] per-warp counts, then bases
   __shared__ int s_wn[kPermWarps + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -650,9 +655,11 @@ __global__ void __launch_bounds__(kPermThreads) k_perm_count(PermuteArgs p, Perm
     s.lrank[f] = local ? wc[warp * E + le] + rank_w : -1;
     s.lpos[f] = local ? s_wn[warp] + __popc(bal & lanemask_lt()) : -1;
   }
+  pdl_trigger();
 }
 
 __global__ void __launch_bounds__(kPermThreads) k_perm_scan(PermuteArgs p, PermuteScratch s) {
+  pdl_wait();
   extern __shared__ __align__(16) int scan_sm[];  // counts [E], offsets [E+1], scratch [E]
   __shared__ int s_warp[33];
   const int E = p.e_local;
@@ -698,11 +705,13 @@ __global__ void __launch_bounds__(kPermThreads) k_perm_scan(PermuteArgs p, Permu
   __syncthreads();
   if (p.tiles1) build_tiles(p, counts, offsets, scratch, s_warp, p.tiles1, p.ntiles1, p.bn1, p.nb1);
   if (p.tiles2) build_tiles(p, counts, offsets, scratch, s_warp, p.tiles2, p.ntiles2, p.bn2, p.nb2);
+  pdl_trigger();
 }
 
 size_t perm_scan_smem_bytes(int e_local) { return (size_t)(3 * e_local + 1) * sizeof(int); }
 
 __global__ void __launch_bounds__(256) k_perm_scatter(PermuteArgs p, PermuteScratch s) {
+  pdl_wait();
   const int P = p.T * p.k;
   const int f = blockIdx.x * blockDim.x + threadIdx.x;
   if (f >= P) return;
@@ -721,6 +730,7 @@ __global__ void __launch_bounds__(256) k_perm_scatter(PermuteArgs p, PermuteScra
   if (p.sort_order) p.sort_order[r] = lp;
   if (p.inverse_order) p.inverse_order[lp] = r;
   if (p.sorted_expert_ids) p.sorted_expert_ids[r] = le;
+  pdl_trigger();
 }
 
 // Groups from an arbitrary per-row expert array (the ragged-GEMM shim): every maximal run
@@ -728,6 +738,7 @@ __global__ void __launch_bounds__(256) k_perm_scatter(PermuteArgs p, PermuteScra
 __global__ void __launch_bounds__(1024) k_tiles_from_runs(const int32_t* __restrict__ m_indices, int M, int bn,
                                                           int nb, int4* __restrict__ tiles, int* __restrict__ ntiles,
                                                           int cap) {
+  pdl_wait();
   __shared__ int s_base;
   __shared__ int s_warp[32];
   if (threadIdx.x == 0) s_base = 0;
@@ -781,6 +792,7 @@ __global__ void __launch_bounds__(1024) k_tiles_from_runs(const int32_t* __restr
     __syncthreads();
   }
   if (threadIdx.x == 0) *ntiles = min(s_base, cap);
+  pdl_trigger();
 }
 
 }  // namespace msv
@@ -788,6 +800,7 @@ __global__ void __launch_bounds__(1024) k_tiles_from_runs(const int32_t* __restr
 namespace msv {
 // Tile list of a dense GEMM: one group of M rows chunked by bn, times nb n-blocks.
 __global__ void k_tiles_dense(int M, int bn, int nb, int4* __restrict__ tiles, int* __restrict__ ntiles) {
+  pdl_wait();
   const int nch = (M + bn - 1) / bn;
   const int n = nch * nb;
   const int cs = ((M + nch - 1) / nch + 15) & ~15;
@@ -797,5 +810,6 @@ __global__ void k_tiles_dense(int M, int bn, int nb, int4* __restrict__ tiles, i
     tiles[i] = make_int4(r0, max(0, min(cs, M - r0)), 0, nbi);
   }
   if (blockIdx.x == 0 && threadIdx.x == 0) *ntiles = n;
+  pdl_trigger();
 }
 }  // namespace msv

@@ -73,6 +73,7 @@ __global__ void __launch_bounds__(128, 1) k_router_gemm(const __grid_constant__ 
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s_tmem;
+  pdl_wait();
   if (warp == 0) {
     if (lane == 0) {
       Ring<kRtStages> st;
@@ -142,6 +143,7 @@ __global__ void __launch_bounds__(128, 1) k_router_gemm(const __grid_constant__ 
     tmem_dealloc(tmem, kRtBN);
   }
   if (threadIdx.x == 0 && s_abort) atomicExch(a.err, (int)MSV_ERR_TIMEOUT);
+  pdl_trigger();
 }
 
 // logits[t][e] = sum over splits s (in order) of part[s][t][e], rounded to bf16 when asked;
@@ -149,6 +151,7 @@ __global__ void __launch_bounds__(128, 1) k_router_gemm(const __grid_constant__ 
 // together.  T * E is a multiple of 4 (E % 16 == 0).
 __global__ void __launch_bounds__(256) k_router_sum_splits(const float* __restrict__ part, int nsplit, int64_t n4,
                                                            int round_bf16, float* __restrict__ logits) {
+  pdl_wait();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n4) return;
   const float4* p = reinterpret_cast<const float4*>(part) + i;
@@ -180,6 +183,7 @@ __global__ void __launch_bounds__(256) k_router_sum_splits(const float* __restri
     acc.w = bf16_round(acc.w);
   }
   reinterpret_cast<float4*>(logits)[i] = acc;
+  pdl_trigger();
 }
 
 }  // namespace msv
