@@ -448,40 +448,48 @@ MSV_DEVICE int block_excl_scan(int v, int* s_warp, int* total) {
 // Tile list of one grouped GEMM: per local expert with c rows, ceil(c/bn) row chunks of
 // near-equal size (multiples of 16) times nb weight n-blocks, ordered expert, n-block, chunk
 // (chunks sharing a weight tile are adjacent).  The shared-expert group goes first.
-MSV_DEVICE void build_tiles(const PermuteArgs& p, const int* counts, const int* offsets, int* scratch, int* s_warp,
+MSV_DEVICE void build_tiles(const PermuteArgs& p, const int* counts, const int* offsets, int4* info, int* s_warp,
                             int4* tiles, int* ntiles, int bn, int nb) {
   const int tid = threadIdx.x;
+  const int E = p.e_local;
   const int nsh_chunks = p.shared_rows > 0 ? (p.shared_rows + bn - 1) / bn : 0;
   const int nsh = nsh_chunks * nb;
-  // per-expert tile counts -> exclusive scan (one expert per thread, e_local <= 1024)
-  const int c_mine = tid < p.e_local ? counts[tid] : 0;
-  const int n_mine = c_mine > 0 ? ((c_mine + bn - 1) / bn) * nb : 0;
+  // per expert (one per thread, e_local <= 1024): chunk count and size, tile count -> scan
+  const int c_mine = tid < E ? counts[tid] : 0;
+  int nch = 0, cs = 0;
+  if (c_mine > 0) {
+    nch = (c_mine + bn - 1) / bn;
+    cs = ((c_mine + nch - 1) / nch + 15) & ~15;
+  }
   int total = 0;
-  const int base_mine = block_excl_scan(n_mine, s_warp, &total);
-  if (tid < p.e_local) scratch[tid] = nsh + base_mine;
+  const int base_mine = block_excl_scan(nch * nb, s_warp, &total);
+  if (tid < E) info[tid] = make_int4(nsh + base_mine, offsets[tid], c_mine, nch | (cs << 16));
   if (tid == 0) *ntiles = nsh + total;
   __syncthreads();
   // shared-expert tiles
   for (int i = tid; i < nsh; i += kPermThreads) {
     int nbi = i / nsh_chunks, ch = i % nsh_chunks;
-    int cs = ((p.shared_rows + nsh_chunks - 1) / nsh_chunks + 15) & ~15;
-    int r0 = ch * cs;
-    int nr = min(cs, p.shared_rows - r0);
+    int scs = ((p.shared_rows + nsh_chunks - 1) / nsh_chunks + 15) & ~15;
+    int r0 = ch * scs;
+    int nr = min(scs, p.shared_rows - r0);
     tiles[i] = make_int4(p.row_base_shared + r0, nr, (1 << 24) | 0, nbi);
   }
-  for (int e = tid; e < p.e_local; e += kPermThreads) {
-    int c = counts[e];
-    if (c == 0) continue;
-    int nch = (c + bn - 1) / bn;
-    int cs = ((c + nch - 1) / nch + 15) & ~15;
-    int base = scratch[e];
-    for (int nbi = 0; nbi < nb; ++nbi)
-      for (int ch = 0; ch < nch; ++ch) {
-        int r0 = ch * cs;
-        int nr = min(cs, c - r0);
-        if (nr <= 0) nr = 0;
-        tiles[base + nbi * nch + ch] = make_int4(offsets[e] + r0, nr, e, nbi);
-      }
+  // one thread per (expert, n-block), so a warp writes an expert's consecutive tiles.
+  // expert = item / nb as a multiply-high by ceil(2^32 / nb): exact while item * nb < 2^32.
+  const uint32_t magic = nb > 1 ? 0xffffffffu / (uint32_t)nb + 1u : 0u;
+  for (int item = tid; item < E * nb; item += kPermThreads) {
+    const int e = nb > 1 ? (int)__umulhi((uint32_t)item, magic) : item;
+    const int4 in = info[e];
+    if (in.z == 0) continue;
+    const int nbi = item - e * nb;
+    const int enc = in.w & 0xffff, ecs = in.w >> 16;
+    const int base = in.x + nbi * enc;
+    for (int ch = 0; ch < enc; ++ch) {
+      const int r0 = ch * ecs;
+      int nr = min(ecs, in.z - r0);
+      if (nr <= 0) nr = 0;
+      tiles[base + ch] = make_int4(in.y + r0, nr, e, nbi);
+    }
   }
   __syncthreads();
 }
@@ -492,7 +500,7 @@ MSV_DEVICE void build_tiles(const PermuteArgs& p, const int* counts, const int* 
 // __match_any_sync, which keeps the sort stable.
 __global__ void __launch_bounds__(kPermThreads) k_permute(PermuteArgs p) {
   pdl_wait();
-  extern __shared__ __align__(16) int hist[];  // [kPermWarps][e_local], then scratch
+  extern __shared__ __align__(16) int hist[];  // [kPermWarps][e_local], counts, offsets
   __shared__ int s_nloc[kPermWarps];
   __shared__ int s_total;
   __shared__ int s_warp[33];
@@ -500,7 +508,6 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermuteArgs p) {
   const int E = p.e_local;
   int* counts = hist + kPermWarps * E;   // [E]
   int* offsets = counts + E;             // [E+1]
-  int* scratch = offsets + E + 1;        // [E]
   const int P = p.T * p.k;
   // counting warps: at least 64 slots each, so small batches sum few per-warp histograms
   const int HW = max(1, min(kPermWarps, (P + 63) / 64));
@@ -583,12 +590,14 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermuteArgs p) {
     const int padded = ((nl + p.alignment - 1) / p.alignment) * p.alignment;
     for (int r = nl + threadIdx.x; r < padded; r += kPermThreads) p.sorted_expert_ids[r] = -1;
   }
-  if (p.tiles1) build_tiles(p, counts, offsets, scratch, s_warp, p.tiles1, p.ntiles1, p.bn1, p.nb1);
-  if (p.tiles2) build_tiles(p, counts, offsets, scratch, s_warp, p.tiles2, p.ntiles2, p.bn2, p.nb2);
+  // the per-warp histogram is dead here: its first 4 * e_local ints hold the per-expert tile info
+  int4* info = reinterpret_cast<int4*>(hist);
+  if (p.tiles1) build_tiles(p, counts, offsets, info, s_warp, p.tiles1, p.ntiles1, p.bn1, p.nb1);
+  if (p.tiles2) build_tiles(p, counts, offsets, info, s_warp, p.tiles2, p.ntiles2, p.bn2, p.nb2);
   pdl_trigger();
 }
 
-size_t permute_smem_bytes(int e_local) { return (size_t)(kPermWarps * e_local + 3 * e_local + 1) * sizeof(int); }
+size_t permute_smem_bytes(int e_local) { return (size_t)(kPermWarps * e_local + 2 * e_local + 1) * sizeof(int); }
 
 // ── multi-block dispatch (large T*k) ──────────────────────────────────────────────────────
 // The same stable counting sort as k_permute, spread over blocks of kPermThreads slots:
@@ -660,12 +669,12 @@ __global__ void __launch_bounds__(kPermThreads) k_perm_count(PermuteArgs p, Perm
 
 __global__ void __launch_bounds__(kPermThreads) k_perm_scan(PermuteArgs p, PermuteScratch s) {
   pdl_wait();
-  extern __shared__ __align__(16) int scan_sm[];  // counts [E], offsets [E+1], scratch [E]
+  extern __shared__ __align__(16) int scan_sm[];  // tile info int4 [E], counts [E], offsets [E+1]
   __shared__ int s_warp[33];
   const int E = p.e_local;
-  int* counts = scan_sm;
+  int4* info = reinterpret_cast<int4*>(scan_sm);
+  int* counts = scan_sm + 4 * E;
   int* offsets = counts + E;
-  int* scratch = offsets + E + 1;
   for (int x = threadIdx.x; x < E; x += kPermThreads) {
     int c = 0;
     for (int b = 0; b < s.nblk; ++b) c += s.blk_hist[b * E + x];
@@ -703,12 +712,12 @@ __global__ void __launch_bounds__(kPermThreads) k_perm_scan(PermuteArgs p, Permu
     for (int r = total + threadIdx.x; r < padded; r += kPermThreads) p.sorted_expert_ids[r] = -1;
   }
   __syncthreads();
-  if (p.tiles1) build_tiles(p, counts, offsets, scratch, s_warp, p.tiles1, p.ntiles1, p.bn1, p.nb1);
-  if (p.tiles2) build_tiles(p, counts, offsets, scratch, s_warp, p.tiles2, p.ntiles2, p.bn2, p.nb2);
+  if (p.tiles1) build_tiles(p, counts, offsets, info, s_warp, p.tiles1, p.ntiles1, p.bn1, p.nb1);
+  if (p.tiles2) build_tiles(p, counts, offsets, info, s_warp, p.tiles2, p.ntiles2, p.bn2, p.nb2);
   pdl_trigger();
 }
 
-size_t perm_scan_smem_bytes(int e_local) { return (size_t)(3 * e_local + 1) * sizeof(int); }
+size_t perm_scan_smem_bytes(int e_local) { return (size_t)(6 * e_local + 1) * sizeof(int); }
 
 __global__ void __launch_bounds__(256) k_perm_scatter(PermuteArgs p, PermuteScratch s) {
   pdl_wait();
