@@ -802,6 +802,8 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
   const bool given = flags & MSV_FWD_ROUTING_GIVEN;
   if (given && (!topk_w || !topk_ids)) return fail(MSV_ERR_INVALID, "msv_moe_forward: routing given but null");
   if (!given && !logits) return fail(MSV_ERR_INVALID, "msv_moe_forward: null router logits");
+  if (!given && L.E > 1024)
+    return fail(MSV_ERR_UNSUPPORTED, "msv_moe_forward: the router takes at most 1024 experts (E=%d)", L.E);
   if (!W->gate_w || !W->up_w || !W->gate_s || !W->up_s || !W->down_w || !W->down_s)
     return fail(MSV_ERR_INVALID, "msv_moe_forward: null routed-expert weight");
   if (L.shared && (!W->sh_gate_w || !W->sh_up_w || !W->sh_down_w || !W->sh_gate_s || !W->sh_up_s || !W->sh_down_s))

@@ -36,43 +36,7 @@ struct Arr {
   }
 };
 
-// ---- sequential libstdc++ pieces (run by one lane) ----------------------------------------
-
-MSV_DEVICE void insertion_sort(Arr a, int f, int l) {
-  if (f == l) return;
-  for (int i = f + 1; i < l; ++i) {
-    float val = a.v[i];
-    uint16_t vix = a.ix[i];
-    if (gt(val, a.v[f])) {
-      for (int j = i; j > f; --j) {
-        a.v[j] = a.v[j - 1];
-        a.ix[j] = a.ix[j - 1];
-      }
-      a.v[f] = val;
-      a.ix[f] = vix;
-    } else {
-      int j = i, n = i - 1;
-      while (gt(val, a.v[n])) {
-        a.v[j] = a.v[n];
-        a.ix[j] = a.ix[n];
-        j = n;
-        --n;
-      }
-      a.v[j] = val;
-      a.ix[j] = vix;
-    }
-  }
-}
-
-MSV_DEVICE void move_median_to_first(Arr a, int r, int x, int y, int z) {
-  if (gt(a.v[x], a.v[y])) {
-    if (gt(a.v[y], a.v[z])) a.swap(r, y);
-    else if (gt(a.v[x], a.v[z])) a.swap(r, z);
-    else a.swap(r, x);
-  } else if (gt(a.v[x], a.v[z])) a.swap(r, x);
-  else if (gt(a.v[y], a.v[z])) a.swap(r, z);
-  else a.swap(r, y);
-}
+// ---- sequential libstdc++ heap pieces (run by one lane) ------------------------------------
 
 MSV_DEVICE void push_heap(Arr a, int base, int hole, int top, float val, uint16_t vix) {
   int parent = (hole - 1) / 2;
@@ -137,61 +101,108 @@ MSV_DEVICE void sort_heap(Arr a, int f, int l) {
   }
 }
 
-// ---- warp-parallel unguarded partition of [lo, hi), pivot value p stored at lo-1 ---------
+// ---- warp-parallel pieces -------------------------------------------------------------------
 
-MSV_DEVICE int warp_partition(Arr a, int lo, int hi, float p, uint16_t* lpos, uint16_t* rpos) {
+// libstdc++'s __insertion_sort over [f, l), l - f <= 32.  For a strict weak order it leaves a
+// stable descending sort: an element moves left only past elements it compares greater than.
+// So each lane takes one element and writes it at its rank: the elements greater than it, plus
+// the equivalent ones before it.
+MSV_DEVICE void warp_insertion_sort(Arr a, int f, int l) {
   const int lane = threadIdx.x & 31;
-  // compact left stops (ascending) and right stops (descending)
-  int nl = 0, nr = 0;
-  for (int base = lo; base < hi; base += 32) {
-    int i = base + lane;
-    bool stop = (i < hi) && !gt(a.v[i], p);
-    uint32_t bal = __ballot_sync(0xffffffffu, stop);
-    if (stop) lpos[nl + __popc(bal & lanemask_lt())] = (uint16_t)i;
-    nl += __popc(bal);
+  const int n = l - f;
+  if (n < 2) return;
+  float x = 0.f;
+  uint16_t xi = 0;
+  if (lane < n) {
+    x = a.v[f + lane];
+    xi = a.ix[f + lane];
   }
-  for (int base = hi - 1; base >= lo - 1; base -= 32) {
-    int j = base - lane;
-    bool stop = (j >= lo - 1) && !gt(p, a.v[j]);
-    uint32_t bal = __ballot_sync(0xffffffffu, stop);
-    if (stop) rpos[nr + __popc(bal & lanemask_lt())] = (uint16_t)j;
-    nr += __popc(bal);
+  int rank = 0;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float y = __shfl_sync(0xffffffffu, x, j);
+    rank += j < n && (gt(y, x) || (j < lane && !gt(x, y)));
+  }
+  for (int j = 16; j < n; ++j) {
+    const float y = __shfl_sync(0xffffffffu, x, j);
+    rank += gt(y, x) || (j < lane && !gt(x, y));
+  }
+  __syncwarp();
+  if (lane < n) {
+    a.v[f + rank] = x;
+    a.ix[f + rank] = xi;
+  }
+  __syncwarp();
+}
+
+// Unguarded partition of [lo, hi) around p, the pivot that the median step moved to lo-1 (the
+// element it displaced, w, moved to position r; lane 0 stores that swap while this runs, so the
+// sweep reads those two positions from registers).  One sweep over the range in 32-element
+// chunks writes the left stops (positions >= lo holding !(x > p)) upward into lpos and the
+// right stops (positions >= lo-1 holding !(p > x)) upward into rposr, so the m-th right stop
+// counted from the top is rposr[nr-1-m].  A second loop swaps the m-th pairs while the left
+// stop lies below the right one; the pairs are disjoint, one per lane.
+MSV_DEVICE int warp_partition(Arr a, int lo, int hi, float p, int r, float w, uint16_t* lpos, uint16_t* rposr) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t lt = lanemask_lt();
+  const int b0 = lo - 1;
+  const int nch = (hi - b0 + 31) >> 5;
+  int nl = 0, nr = 0;
+  // four chunks per step: their loads issue together, before any store of the step
+  for (int c0 = 0; c0 < nch; c0 += 4) {
+    float xs[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = b0 + 32 * (c0 + u) + lane;
+      xs[u] = i < hi ? a.v[i] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = b0 + 32 * (c0 + u) + lane;
+      const bool in = i < hi;
+      const float x = i == r ? w : (i == b0 ? p : xs[u]);
+      const bool sl = in && i >= lo && !gt(x, p);
+      const bool sr = in && !gt(p, x);
+      const uint32_t bl = __ballot_sync(0xffffffffu, sl);
+      const uint32_t br = __ballot_sync(0xffffffffu, sr);
+      if (sl) lpos[nl + __popc(bl & lt)] = (uint16_t)i;
+      if (sr) rposr[nr + __popc(br & lt)] = (uint16_t)i;
+      nl += __popc(bl);
+      nr += __popc(br);
+    }
   }
   __syncwarp();
   // swaps happen for the prefix of m with lpos[m] < rpos[m] (monotone in m)
   const int mmax = min(nl, nr);
   int nsw = 0;
-  for (int base = 0; base < mmax; base += 32) {
-    int m = base + lane;
-    bool sw = (m < mmax) && (lpos[m] < rpos[m]);
-    nsw += __popc(__ballot_sync(0xffffffffu, sw));
+  int Ln = 0, Rn = 0;  // the next step's pair, loaded ahead of this step's swaps
+  if (lane < mmax) {
+    Ln = lpos[lane];
+    Rn = rposr[nr - 1 - lane];
   }
-  // perform the swaps (disjoint positions)
-  for (int base = 0; base < nsw; base += 32) {
-    int m = base + lane;
-    float lv = 0.f, rv = 0.f;
-    uint16_t li = 0, ri = 0;
-    int L = 0, R = 0;
-    if (m < nsw) {
-      L = lpos[m];
-      R = rpos[m];
-      lv = a.v[L];
-      li = a.ix[L];
-      rv = a.v[R];
-      ri = a.ix[R];
+  for (int base = 0; base < mmax; base += 32) {
+    const int m = base + lane;
+    const int L = Ln, R = Rn;
+    if (m + 32 < mmax) {
+      Ln = lpos[m + 32];
+      Rn = rposr[nr - 33 - m];
     }
-    __syncwarp();
-    if (m < nsw) {
+    const bool sw = m < mmax && L < R;
+    const uint32_t bal = __ballot_sync(0xffffffffu, sw);
+    if (sw) {
+      const float lv = a.v[L], rv = a.v[R];
+      const uint16_t li = a.ix[L], ri = a.ix[R];
       a.v[L] = rv;
       a.ix[L] = ri;
       a.v[R] = lv;
       a.ix[R] = li;
     }
-    __syncwarp();
+    nsw += __popc(bal);
+    if (bal != 0xffffffffu) break;
   }
   int cut = 0x7fffffff;
   if (nsw < nl) cut = lpos[nsw];
-  if (nsw >= 1) cut = min(cut, (int)rpos[nsw - 1]);
+  if (nsw >= 1) cut = min(cut, (int)rposr[nr - nsw]);
   __syncwarp();
   return cut;
 }
@@ -203,54 +214,69 @@ MSV_DEVICE int warp_partition(Arr a, int lo, int hi, float p, uint16_t* lpos, ui
 // result to positions [0,k) and returns true, or returns false with the row untouched (the
 // replay below then decides the order of the tied values).  Rows holding a NaN never come here.
 constexpr int kFastTopkMax = 512;
+
+// order-preserving map of a non-NaN float onto uint32 (larger float -> larger key; -0 and +0,
+// which compare equal, share a key)
+MSV_DEVICE uint32_t f32_order_key(float x) {
+  const uint32_t u = x == 0.f ? 0u : __float_as_uint(x);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
 __device__ __noinline__ bool warp_topk_distinct(Arr a, int n, int k) {
   if (n > kFastTopkMax) return false;
   const int lane = threadIdx.x & 31;
   const int rounds = k < n ? k + 1 : k;
   constexpr int NV = kFastTopkMax / 32;
-  float x[NV];
-  uint32_t taken = 0;  // bit j: element lane + 32 j selected or absent
+  // order keys of the lane's values i = lane + 32 j; 0 marks taken or absent (no real key is 0)
+  uint32_t kx[NV];
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
     const int i = lane + 32 * j;
-    if (i < n) x[j] = a.v[i];
-    else {
-      x[j] = 0.f;
-      taken |= 1u << j;
-    }
+    kx[j] = i < n ? f32_order_key(a.v[i]) : 0u;
   }
-  float sel_v = 0.f, prev = 0.f;
+  // the lane's largest remaining key and its slot, by a pairwise tree (depth log2 NV)
+  auto lane_best = [&](uint32_t& bk, int& bj) {
+    uint32_t tk[NV];
+    int tj[NV];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      tk[j] = kx[j];
+      tj[j] = j;
+    }
+#pragma unroll
+    for (int w = NV / 2; w >= 1; w >>= 1)
+#pragma unroll
+      for (int j = 0; j < w; ++j) {
+        const bool hi = tk[j + w] > tk[j];
+        tk[j] = hi ? tk[j + w] : tk[j];
+        tj[j] = hi ? tj[j + w] : tj[j];
+      }
+    bk = tk[0];
+    bj = tj[0];
+  };
+  uint32_t mk;
+  int mj;
+  lane_best(mk, mj);
+  uint32_t prev = 0;
   int sel_i = 0;
   for (int r = 0; r < rounds; ++r) {
-    float best = 0.f;
-    int bj = -1;
+    const uint32_t kmax = __reduce_max_sync(0xffffffffu, mk);
+    const uint32_t holders = __ballot_sync(0xffffffffu, mk == kmax);
+    // two lanes holding the maximum, or a maximum equal to the previous one, is a tie among
+    // the k+1 largest (a tie found only in the last round lies below the selection)
+    if ((r + 1 < rounds && __popc(holders) > 1) || (r > 0 && !(prev > kmax))) return false;
+    prev = kmax;
+    const int wl = __ffs(holders) - 1;
+    const int bi = __shfl_sync(0xffffffffu, wl + 32 * mj, wl);
+    if (lane == r) sel_i = bi;
+    if (lane == wl) {
 #pragma unroll
-    for (int j = 0; j < NV; ++j)
-      if (!((taken >> j) & 1u) && (bj < 0 || x[j] > best)) {
-        best = x[j];
-        bj = j;
-      }
-    int bi = bj < 0 ? 0x7fffffff : lane + 32 * bj;
-    int have = bj >= 0;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      const int oh = __shfl_xor_sync(0xffffffffu, have, o);
-      if (oh && (!have || ob > best || (ob == best && oi < bi))) {
-        best = ob;
-        bi = oi;
-        have = oh;
-      }
-    }
-    if (r > 0 && !(prev > best)) return false;  // a tie (warp-uniform: all lanes hold the same pair)
-    prev = best;
-    if (lane == (bi & 31)) taken |= 1u << (bi >> 5);
-    if (lane == r) {
-      sel_v = best;
-      sel_i = bi;
+      for (int j = 0; j < NV; ++j)
+        if (j == mj) kx[j] = 0u;
+      lane_best(mk, mj);
     }
   }
+  const float sel_v = lane < k ? a.v[sel_i] : 0.f;
   __syncwarp();
   if (lane < k) {
     a.v[lane] = sel_v;
@@ -286,23 +312,40 @@ MSV_DEVICE void warp_topk_torch_cpu(Arr a, int n, int k, uint16_t* lpos, uint16_
       break;
     }
     depth--;
+    // libstdc++ __move_median_to_first(f, f+1, mid, l-1): every lane reads the candidates and
+    // picks the same one, r; lane 0 swaps it with position f
     const int mid = f + (l - f) / 2;
-    if (lane == 0) move_median_to_first(a, f, f + 1, mid, l - 1);
+    const float vf = a.v[f], vx = a.v[f + 1], vy = a.v[mid], vz = a.v[l - 1];
+    const uint16_t jf = a.ix[f], jx = a.ix[f + 1], jy = a.ix[mid], jz = a.ix[l - 1];
+    int r;
+    float p;
+    uint16_t jr;
+    if (gt(vx, vy)) {
+      if (gt(vy, vz)) r = mid, p = vy, jr = jy;
+      else if (gt(vx, vz)) r = l - 1, p = vz, jr = jz;
+      else r = f + 1, p = vx, jr = jx;
+    } else if (gt(vx, vz)) r = f + 1, p = vx, jr = jx;
+    else if (gt(vy, vz)) r = l - 1, p = vz, jr = jz;
+    else r = mid, p = vy, jr = jy;
     __syncwarp();
-    const float p = a.v[f];
-    const int cut = warp_partition(a, f + 1, l, p, lpos, rpos);
+    if (lane == 0) {
+      a.v[f] = p;
+      a.ix[f] = jr;
+      a.v[r] = vf;
+      a.ix[r] = jf;
+    }
+    const int cut = warp_partition(a, f + 1, l, p, r, vf, lpos, rpos);
     if (cut <= nth) f = cut;
     else l = cut;
   }
-  if (lane == 0) {
-    if (!done) insertion_sort(a, f, l);
-    // std::sort(first, first + k - 1): k - 1 <= 16 elements, i.e. one insertion sort
-    insertion_sort(a, 0, k - 1);
-  }
   __syncwarp();
+  if (!done) warp_insertion_sort(a, f, l);  // l - f <= 3
+  // std::sort(first, first + k - 1): k - 1 <= 16 elements, i.e. one insertion sort
+  warp_insertion_sort(a, 0, k - 1);
 }
 
 constexpr int kRouteWarps = 4;
+constexpr int kRouteMaxE = 1024;  // the host entry points reject larger rows
 
 // One warp per token.  Shared memory per warp: n floats + 3n uint16.
 __global__ void __launch_bounds__(kRouteWarps * 32) k_route_topk(const float* __restrict__ logits, int64_t ld,
@@ -324,14 +367,23 @@ __global__ void __launch_bounds__(kRouteWarps * 32) k_route_topk(const float* __
   float mx = -INFINITY;
   bool any_nan = false;
   uint32_t low_bits = 0;  // zero when every value of the row is a bf16 value
-#pragma unroll 8
-  for (int i = lane; i < E; i += 32) {
-    float x = row[i];
-    v[i] = x;
-    ix[i] = (uint16_t)i;
-    mx = fmaxf(mx, x);
-    any_nan |= (x != x);
-    low_bits |= __float_as_uint(x) & 0xffffu;
+  float xr[kRouteMaxE / 32];  // the lane's values i = lane + 32 j (E <= kRouteMaxE)
+#pragma unroll
+  for (int j = 0; j < kRouteMaxE / 32; ++j) {
+    const int i = lane + 32 * j;
+    xr[j] = i < E ? row[i] : 0.f;
+  }
+#pragma unroll
+  for (int j = 0; j < kRouteMaxE / 32; ++j) {
+    const int i = lane + 32 * j;
+    if (i < E) {
+      const float x = xr[j];
+      v[i] = x;
+      ix[i] = (uint16_t)i;
+      mx = fmaxf(mx, x);
+      any_nan |= (x != x);
+      low_bits |= __float_as_uint(x) & 0xffffu;
+    }
   }
   mx = warp_max(mx);
   any_nan = __any_sync(0xffffffffu, any_nan);
@@ -343,7 +395,9 @@ __global__ void __launch_bounds__(kRouteWarps * 32) k_route_topk(const float* __
   const bool all_nan = softmax && (any_nan || mx == INFINITY);
   float sum = 0.f;
   if (softmax && !all_nan) {
-    for (int i = lane; i < E; i += 32) sum += expf(v[i] - mx);
+#pragma unroll
+    for (int j = 0; j < kRouteMaxE / 32; ++j)
+      if (lane + 32 * j < E) sum += expf(xr[j] - mx);
     sum = warp_sum(sum);
   }
   if (all_nan)
@@ -360,8 +414,13 @@ __global__ void __launch_bounds__(kRouteWarps * 32) k_route_topk(const float* __
     s = softmax ? (all_nan ? x : expf(x - mx) * (1.0f / sum)) : x;
   }
   if (renorm) {
+    float sj[16];  // k <= 16; all shuffles issue first, then the sum runs in slot order
+#pragma unroll
+    for (int j = 0; j < 16; ++j) sj[j] = __shfl_sync(0xffffffffu, s, j);
     float tot = 0.f;
-    for (int j = 0; j < k; ++j) tot += __shfl_sync(0xffffffffu, s, j);  // slot order
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (j < k) tot += sj[j];
     s = __fdiv_rn(s, tot);
   }
   if (lane < k) {

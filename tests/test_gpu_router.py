@@ -51,6 +51,33 @@ def test_router_tie_heavy_bf16_logits(cuda, E, k, T):
     torch.testing.assert_close(w.cpu(), ref_w, rtol=2e-6, atol=1e-7)
 
 
+@pytest.mark.parametrize("E,k", [(512, 10), (256, 8), (64, 6), (16, 16)])
+def test_router_fp32_rows_with_planted_ties(cuda, E, k):
+    """fp32 logits: distinct rows take the register fast path, rows with a tie among the k+1
+    largest (signed zeros included) fall back to the replay; both must match torch."""
+    g = torch.Generator().manual_seed(E * 7 + k)
+    T = 64
+    x = torch.randn(T, E, generator=g)
+    for t in range(T):
+        order = torch.argsort(x[t], descending=True)
+        kind = t % 5
+        if kind == 1:  # the two largest are +0 and -0
+            x[t] = -x[t].abs() - 0.1
+            x[t, order[3]] = 0.0
+            x[t, order[E // 2]] = -0.0
+        elif kind == 2 and k < E:  # tie between ranks k-1 and k
+            x[t, order[k]] = x[t, order[k - 1]]
+        elif kind == 3:  # tie at the top
+            x[t, order[1]] = x[t, order[0]]
+        elif kind == 4 and k + 1 < E:  # tie just below the selection
+            x[t, order[k + 1]] = x[t, order[k]]
+    w, ids = moe.route_topk(x.to(cuda), k, w_dtype=torch.float32)
+    ref_w, ref_ids = torch.topk(torch.softmax(x, -1), k, -1)
+    ref_w = ref_w / ref_w.sum(-1, keepdim=True)
+    assert torch.equal(ids.cpu(), ref_ids)
+    torch.testing.assert_close(w.cpu(), ref_w, rtol=2e-6, atol=1e-7)
+
+
 def test_topk_select_on_cpu_scores_is_exact(cuda):
     """Given the very same fp32 scores, the ids equal torch.topk's, whatever the ties."""
     g = torch.Generator().manual_seed(5)
