@@ -9,6 +9,8 @@ N > 1  -> BASELINE config 3 (launched by torchrun, one rank per GPU): the same l
           with the expert intermediate sharded (column-parallel gate_up, row-parallel down),
           256 tokens, per-rank partial [256,4096] bf16 summed by one NCCL all-reduce.
 --workload prefill -> BASELINE config 2 on one GPU (8192 tokens, router GEMM on cuBLAS).
+--workload stack   -> BASELINE config 4: the 60-layer MoE decode stack (128 tokens, Zipf(1.2)
+          logit prior, RMSNorm + router GEMM + layer per layer) as one CUDA graph at TP=N.
 
 Synthetic seeded data, random-init weights of the full shape.  Timed region: K steps between
 barrier + synchronize, CUDA events on the launching stream, max over ranks.  Every step
@@ -380,6 +382,141 @@ def run_ours(args, world, rank, local):
         emit(res)
 
 
+def run_stack(args, world, rank, local):
+    """the 60-layer MoE-only decode stack at TP=N (the decoder's MoE half per
+    layer, attention/GDN taken as identity): ``h <- h + moe_l(rms_norm_gemma(h))`` with the
+    router from the normed hidden states, a Zipf(1.2) expert-popularity prior added to each
+    layer's router logits, the intermediate sharded over the ranks and one NCCL all-reduce per
+    layer.  The whole step is one CUDA graph.  Layers that do not fit in this GPU's memory are
+    dropped (the line reports how many ran)."""
+    from muserve_b200 import _lib, moe, synthetic
+    from muserve_b200.graph import GraphedMoEStack
+    lib = _lib.load()
+    dev = torch.device("cuda", local)
+    tp = world
+    tokens = args.tokens or 128
+    inter, shared = INTER // tp, SHARED // tp
+    per_layer = (E + 1) * expert_bytes(inter) + E * H * 2 + 4 * H + 4 * E
+    free, _ = torch.cuda.mem_get_info(dev)
+    fit = int((free - 16e9) // per_layer)
+    n_layers = int(-max_over_ranks(-float(min(args.layers, fit))))
+    if n_layers < 1:
+        raise RuntimeError("no layer fits in GPU memory")
+    layers, biases = [], []
+    for li in range(n_layers):
+        # this rank's shard of layer li; the router, the shared-expert gate and the norm weight
+        # are the same on every rank (rank-independent seed)
+        w = synthetic.make_layer_weights(H, E, inter, shared, seed=10_000 + 100 * li + rank, device=dev)
+        g = torch.Generator(device=dev).manual_seed(20_000 + li)
+        w["moe.gate.weight"] = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        w["moe.shared_expert_gate.weight"] = (torch.randn(1, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        w["post_attention_layernorm.weight"] = (torch.randn(H, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+        layers.append(w)
+        biases.append(synthetic.zipf_bias(E, 1.2, seed=30_000 + li, device=dev))
+    torch.cuda.synchronize()
+    barrier()
+    x = synthetic.make_hidden(tokens, H, seed=2, device=dev)
+    stack = GraphedMoEStack(layers, batch_size=tokens, top_k=K_TOP, device=dev, norm=True, logit_biases=biases)
+    # routing statistics and this library's launches per step, from one eager step
+    routing = []
+    n0 = moe.launch_count()
+    stack.eager(x, routing=routing)
+    launches_per_step = moe.launch_count() - n0
+    torch.cuda.synchronize()
+    touched = [int((torch.bincount(ids.flatten().long(), minlength=E) > 0).sum().item()) for ids in routing]
+    top_share = statistics.mean(
+        float(torch.bincount(ids.flatten().long(), minlength=E).max().item()) / ids.numel() for ids in routing)
+    stack.capture(x)
+    stream = torch.cuda.current_stream(dev)  # replays, timing events and copies all run here
+    try:
+        for _ in range(args.warmup):
+            stack.run(x)
+        torch.cuda.synchronize()
+        _lib.check(lib.msv_check_device_error(stream.cuda_stream), "warmup")
+        barrier()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        w0.record(stream)
+        stack.graph.replay()
+        w1.record(stream)
+        torch.cuda.synchronize()
+        est_ms = max(w0.elapsed_time(w1), 1e-3)
+        n_soak = int(max_over_ranks(min(2000, max(0, int(args.clock_window_ms / est_ms) - args.steps))))
+        barrier()
+        torch.cuda.synchronize()
+        with Clocks(local) as clk:
+            clk.mark(True)
+            for _ in range(n_soak):
+                stack.graph.replay()
+            t0.record(stream)
+            for _ in range(args.steps):
+                stack.graph.replay()
+            t1.record(stream)
+            torch.cuda.synchronize()
+            clk.mark(False)
+        barrier()
+        ms_total = max_over_ranks(t0.elapsed_time(t1))
+        _lib.check(lib.msv_check_device_error(stream.cuda_stream), "timed region")
+        # e2e through the public API: pinned host input copied in, output read back, every step
+        e2e = None
+        if not args.no_e2e:
+            hx = x.cpu().pin_memory()
+            ho = torch.empty(tokens, H, dtype=torch.bfloat16).pin_memory()
+            dx = torch.empty_like(x)
+
+            def e2e_step():
+                dx.copy_(hx, non_blocking=True)
+                o = stack.run(dx)
+                ho.copy_(o, non_blocking=True)
+            for _ in range(args.warmup):
+                e2e_step()
+            barrier()
+            torch.cuda.synchronize()
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a0.record(stream)
+            for _ in range(args.steps):
+                e2e_step()
+            a1.record(stream)
+            torch.cuda.synchronize()
+            barrier()
+            ms_e2e = max_over_ranks(a0.elapsed_time(a1))
+            e2e = {"value": tokens * args.steps / (ms_e2e / 1e3), "unit": "tokens/s",
+                   "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": ho.numel() * 2,
+                   "ms_per_step": ms_e2e / args.steps}
+    finally:
+        stack.close()  # the graph holds NCCL calls: release it before the process group goes
+    ms_step = ms_total / args.steps
+    hbm, _, peak_kind = peaks()
+    step_bytes = sum(n * expert_bytes(inter) for n in touched) + n_layers * (
+        expert_bytes(shared) + E * H * 2 + 4 * tokens * H * 2)
+    gbs = step_bytes / (ms_step / 1e3) / 1e9
+    res = {
+        "metric": "60-layer MoE decode stack tokens/s", "value": tokens * args.steps / (ms_total / 1e3),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "e4m3 x e4m3 -> fp32 acc, bf16 io",
+        "data": "synthetic (seeded N(0,1) hidden, N(0,0.02) block-quantised weights, Zipf(1.2) logit prior)",
+        "config": {"workload": f"stack{n_layers}_tp{tp}_c4", "layers": n_layers, "layers_requested": args.layers,
+                   "tokens": tokens, "hidden": H, "experts": E, "top_k": K_TOP, "inter_per_rank": inter,
+                   "tp": tp, "parallelism": f"tp{tp}" if tp > 1 else "single",
+                   "graph": "one CUDA graph per step (norm, router GEMM, top-k, dispatch, quantise, 2 GEMMs, "
+                            "combine, NCCL all-reduce per layer)",
+                   "l2": f"no flush: each step streams {step_bytes / 1e9:.1f} GB per rank (> 126 MB L2)"},
+        "step": {"ms": ms_step, "ms_per_layer": ms_step / n_layers, "hbm_gbs": gbs, "hbm_frac": gbs / hbm,
+                 "peak_kind": peak_kind, "mean_touched_experts": statistics.mean(touched),
+                 "mean_top_expert_share": top_share},
+        "roofline": {"bound": "hbm", "kernel": "whole step (graph)", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                     "frac": gbs / hbm, "peak_kind": peak_kind, "traffic": None},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": dict(clk.summary(), window=f"timed region + {n_soak} identical untimed steps just before it"),
+        "e2e": e2e,
+        "cpu_baseline": None,
+    }
+    if rank == 0:
+        emit(res)
+
+
 def cpu_baseline(x, logits, w, tokens):
     """The reference's algorithm on the host cores (the CPU oracle port, all threads), on
     ``tokens`` tokens of the same workload with their GPU routing.  Only the touched routed
@@ -491,7 +628,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "stack"])
+    ap.add_argument("--layers", type=int, default=60, help="layers of the stack workload")
     ap.add_argument("--tokens", type=int, default=0)
     ap.add_argument("--experts", type=int, default=0, help="smaller expert count, for profiler captures only")
     ap.add_argument("--no-e2e", action="store_true")
@@ -507,7 +645,10 @@ def main():
         return
     world, rank, local = setup_dist()
     try:
-        run_ours(args, world, rank, local)
+        if args.workload == "stack":
+            run_stack(args, world, rank, local)
+        else:
+            run_ours(args, world, rank, local)
     finally:
         if dist.is_initialized():
             dist.destroy_process_group()

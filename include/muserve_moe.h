@@ -38,6 +38,12 @@ const char* msv_last_error(void);
 int msv_version(void);
 
 /*
+ * Number of kernels this library has launched in this process (host-side count, one per
+ * launch call; a CUDA-graph replay launches the captured kernels without counting again).
+ */
+unsigned long long msv_launch_count(void);
+
+/*
  * Router: softmax over E fp32 logits, top-k, optional renormalisation of the k weights.
  *   replaces: muserve/model/qwen35_layer_v2.py:569-572 (softmax, torch.topk, /sum, .to(bf16))
  *             muserve/kernels/moe_dispatch.py:20-24 (moe_gate after the fp32 logits GEMM)
@@ -68,6 +74,32 @@ size_t msv_router_workspace_size(int T, int H, int E);
 int msv_router_from_hidden(const void* hidden, const void* gate_w, int T, int H, int E, int k, int renormalize,
                            int round_logits_bf16, void* topk_w, int w_dtype, void* topk_ids, int ids_dtype,
                            float* logits_out, void* workspace, size_t workspace_bytes, msv_stream_t stream);
+
+/*
+ * msv_router_from_hidden with an additive prior on the logits: the routing reads
+ * logits[t,e] + logit_bias[e] (fp32 add after the optional bf16 rounding); logits_out still
+ * receives the GEMM's logits.  logit_bias: [E] fp32, not NULL.  The reference has no such
+ * term; it carries the expert-popularity prior of the 60-layer stack benchmark (Zipf(1.2) log
+ * probabilities added to the router logits).
+ */
+int msv_router_from_hidden_bias(const void* hidden, const void* gate_w, int T, int H, int E, int k, int renormalize,
+                                int round_logits_bf16, const float* logit_bias, void* topk_w, int w_dtype,
+                                void* topk_ids, int ids_dtype, float* logits_out, void* workspace,
+                                size_t workspace_bytes, msv_stream_t stream);
+
+/*
+ * Gemma-style RMSNorm of the residual stream, with the residual add before it fused in.
+ *   replaces: muserve/model/qwen35_layer_v2.py:59-62 (rms_norm_gemma) as the decoder layer
+ *             calls it at :713-714 (x2 = rms_norm_gemma(h, post_attention_layernorm.weight)),
+ *             and the residual add h_flat + moe_out at :715
+ * h: [T,H] bf16, in/out.  add: [T,H] bf16 or NULL; when given, first h <- bf16(h + add).
+ * weight: [H] bf16, stored as an offset from 1.0.  out: [T,H] bf16, or NULL to do the add only
+ * (then add must be given).
+ * out = bf16(h * rstd * bf16(1 + weight)), rstd = 1 / sqrt(mean(h^2) + eps), in fp32 with one
+ * rounding, as torch's rms_norm on bf16.  H % 8 == 0, H <= 16384, pointers 16-byte aligned.
+ */
+int msv_add_rms_norm_gemma(void* h, const void* add, const void* weight, int T, int H, float eps, void* out,
+                           msv_stream_t stream);
 
 /*
  * Top-k selection only, on given fp32 values (no softmax): torch.topk(values, k) order.

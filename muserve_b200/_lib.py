@@ -41,11 +41,14 @@ class MoeWeights(ctypes.Structure):
 _SIGS = {
     "msv_last_error": (ctypes.c_char_p, []),
     "msv_version": (I, []),
+    "msv_launch_count": (ctypes.c_ulonglong, []),
     "msv_check_device_error": (I, [P]),
     "msv_route_topk": (I, [P, I64, I, I, I, I, P, I, P, I, P]),
     "msv_topk_select": (I, [P, I64, I, I, I, P, I, P, P]),
     "msv_router_workspace_size": (SZ, [I, I, I]),
     "msv_router_from_hidden": (I, [P, P, I, I, I, I, I, I, P, I, P, I, P, P, SZ, P]),
+    "msv_router_from_hidden_bias": (I, [P, P, I, I, I, I, I, I, P, P, I, P, I, P, P, SZ, P]),
+    "msv_add_rms_norm_gemma": (I, [P, P, P, I, I, ctypes.c_float, P, P]),
     "msv_moe_permute": (I, [P, I, I, I, I, I, I, I, I, P, P, P, P, P, P]),
     "msv_fp8_quant_128": (I, [P, I64, I, I, P, P, I64, P, I64, I64, P]),
     "msv_ragged_gemm_workspace_size": (SZ, [I, I]),

@@ -13,6 +13,7 @@
 #include "grouped_gemm_rows.cuh"
 #include "quant_combine.cuh"
 #include "route.cuh"
+#include "norm.cuh"
 #include "router_gemm.cuh"
 
 namespace msv {
@@ -383,6 +384,8 @@ int msv_check_device_error(msv_stream_t stream) {
   return MSV_OK;
 }
 
+unsigned long long msv_launch_count(void) { return g_launch_count.load(std::memory_order_relaxed); }
+
 int msv_route_topk(const float* logits, int64_t ld, int T, int E, int k, int renormalize, void* topk_w, int w_dtype,
                    void* topk_ids, int ids_dtype, msv_stream_t stream) {
   if (!logits || !topk_ids || T < 0 || E < 1 || E > 1024 || k < 1 || k > 16 || k > E || ld < E)
@@ -392,7 +395,7 @@ int msv_route_topk(const float* logits, int64_t ld, int T, int E, int k, int ren
   if (T == 0) return MSV_OK;
   const size_t sm = route_smem_bytes(E);
   launch_k(k_route_topk, dim3((T + kRouteWarps - 1) / kRouteWarps), dim3(kRouteWarps * 32), sm, stream, 
-      logits, ld, T, E, k, 1, renormalize, topk_w, w_dtype, topk_ids, ids_dtype, nullptr);
+      logits, ld, T, E, k, 1, renormalize, topk_w, w_dtype, topk_ids, ids_dtype, nullptr, nullptr);
   return cuda_check(cudaGetLastError(), "launch route_topk");
 }
 
@@ -422,9 +425,11 @@ size_t msv_router_workspace_size(int T, int H, int E) {
   return ((size_t)router_splits(T, H, E, nsm) + 1) * (size_t)(T > 0 ? T : 1) * (size_t)E * sizeof(float) + 512;
 }
 
-int msv_router_from_hidden(const void* hidden, const void* gate_w, int T, int H, int E, int k, int renormalize,
-                           int round_logits_bf16, void* topk_w, int w_dtype, void* topk_ids, int ids_dtype,
-                           float* logits_out, void* workspace, size_t workspace_bytes, msv_stream_t stream) {
+namespace {
+int router_from_hidden_impl(const void* hidden, const void* gate_w, int T, int H, int E, int k, int renormalize,
+                            int round_logits_bf16, const float* logit_bias, void* topk_w, int w_dtype, void* topk_ids,
+                            int ids_dtype, float* logits_out, void* workspace, size_t workspace_bytes,
+                            msv_stream_t stream) {
   if (!hidden || !gate_w || !topk_ids || T < 0 || H <= 0 || H % 64 || E < 16 || E % 16 || E > 1024 || k < 1 ||
       k > 16 || k > E)
     return fail(MSV_ERR_INVALID,
@@ -477,8 +482,40 @@ int msv_router_from_hidden(const void* hidden, const void* gate_w, int T, int H,
     if (int rc = cuda_check(cudaGetLastError(), "launch router_sum_splits")) return rc;
   }
   launch_k(k_route_topk, dim3((T + kRouteWarps - 1) / kRouteWarps), dim3(kRouteWarps * 32), route_smem_bytes(E), stream, 
-      logits, E, T, E, k, 1, renormalize, topk_w, w_dtype, topk_ids, ids_dtype, nullptr);
+      logits, E, T, E, k, 1, renormalize, topk_w, w_dtype, topk_ids, ids_dtype, nullptr, logit_bias);
   return cuda_check(cudaGetLastError(), "launch route_topk");
+}
+}  // namespace
+
+int msv_router_from_hidden(const void* hidden, const void* gate_w, int T, int H, int E, int k, int renormalize,
+                           int round_logits_bf16, void* topk_w, int w_dtype, void* topk_ids, int ids_dtype,
+                           float* logits_out, void* workspace, size_t workspace_bytes, msv_stream_t stream) {
+  return router_from_hidden_impl(hidden, gate_w, T, H, E, k, renormalize, round_logits_bf16, nullptr, topk_w, w_dtype,
+                                 topk_ids, ids_dtype, logits_out, workspace, workspace_bytes, stream);
+}
+
+int msv_router_from_hidden_bias(const void* hidden, const void* gate_w, int T, int H, int E, int k, int renormalize,
+                                int round_logits_bf16, const float* logit_bias, void* topk_w, int w_dtype,
+                                void* topk_ids, int ids_dtype, float* logits_out, void* workspace,
+                                size_t workspace_bytes, msv_stream_t stream) {
+  if (!logit_bias) return fail(MSV_ERR_INVALID, "msv_router_from_hidden_bias: null logit_bias");
+  return router_from_hidden_impl(hidden, gate_w, T, H, E, k, renormalize, round_logits_bf16, logit_bias, topk_w,
+                                 w_dtype, topk_ids, ids_dtype, logits_out, workspace, workspace_bytes, stream);
+}
+
+int msv_add_rms_norm_gemma(void* h, const void* add, const void* weight, int T, int H, float eps, void* out,
+                           msv_stream_t stream) {
+  if (!h || T < 0 || H <= 0 || H % 8 || H > 8 * kNormMaxVec * kNormThreads || (out && !weight) || (!out && !add))
+    return fail(MSV_ERR_INVALID, "msv_add_rms_norm_gemma: bad arguments (T=%d H=%d; H %% 8 == 0, H <= %d)", T, H,
+                8 * kNormMaxVec * kNormThreads);
+  if (!is_pow2_aligned(h, 16) || (add && !is_pow2_aligned(add, 16)) || (weight && !is_pow2_aligned(weight, 16)) ||
+      (out && !is_pow2_aligned(out, 16)))
+    return fail(MSV_ERR_INVALID, "msv_add_rms_norm_gemma: pointers must be 16-byte aligned");
+  if (T == 0) return MSV_OK;
+  launch_k(k_add_rms_norm, dim3(T), dim3(kNormThreads), 0, stream, static_cast<__nv_bfloat16*>(h),
+           static_cast<const __nv_bfloat16*>(add), static_cast<const __nv_bfloat16*>(weight),
+           static_cast<__nv_bfloat16*>(out), H, eps);
+  return cuda_check(cudaGetLastError(), "launch add_rms_norm");
 }
 
 int msv_topk_select(const float* values, int64_t ld, int T, int E, int k, void* topk_ids, int ids_dtype,
@@ -488,7 +525,7 @@ int msv_topk_select(const float* values, int64_t ld, int T, int E, int k, void* 
   if (ids_dtype != MSV_I32 && ids_dtype != MSV_I64) return fail(MSV_ERR_INVALID, "msv_topk_select: ids dtype");
   if (T == 0) return MSV_OK;
   launch_k(k_route_topk, dim3((T + kRouteWarps - 1) / kRouteWarps), dim3(kRouteWarps * 32), route_smem_bytes(E), stream, 
-      values, ld, T, E, k, 0, 0, nullptr, MSV_F32, topk_ids, ids_dtype, out_values);
+      values, ld, T, E, k, 0, 0, nullptr, MSV_F32, topk_ids, ids_dtype, out_values, nullptr);
   return cuda_check(cudaGetLastError(), "launch topk_select");
 }
 
@@ -828,7 +865,7 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
   if (int rc = mark(0)) return rc;
   if (!given) {
     launch_k(k_route_topk, dim3((L.T + kRouteWarps - 1) / kRouteWarps), dim3(kRouteWarps * 32), route_smem_bytes(L.E), stream, 
-        logits, L.E, L.T, L.E, L.k, 1, 1, rw, s->weights_dtype, ids, MSV_I32, nullptr);
+        logits, L.E, L.T, L.E, L.k, 1, 1, rw, s->weights_dtype, ids, MSV_I32, nullptr, nullptr);
     if (int rc = cuda_check(cudaGetLastError(), "launch route_topk")) return rc;
   }
   // 2. dispatch bookkeeping + tile lists

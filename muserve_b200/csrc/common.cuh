@@ -9,6 +9,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "../../include/muserve_moe.h"
 
 #define MSV_DEVICE __device__ __forceinline__
@@ -29,9 +31,13 @@ __device__ __forceinline__ float bf16_bits_to_f32(uint32_t w, int hi) {
 MSV_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 MSV_DEVICE void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Host-side count of the kernels this library has launched (msv_launch_count).
+inline std::atomic<unsigned long long> g_launch_count{0};
+
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
                             Args&&... args) {
+  g_launch_count.fetch_add(1, std::memory_order_relaxed);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;

@@ -352,7 +352,8 @@ __global__ void __launch_bounds__(kRouteWarps * 32) k_route_topk(const float* __
                                                                   int T, int E, int k, int softmax, int renorm,
                                                                   void* __restrict__ out_w, int w_dtype,
                                                                   void* __restrict__ out_ids, int ids_dtype,
-                                                                  float* __restrict__ out_vals) {
+                                                                  float* __restrict__ out_vals,
+                                                                  const float* __restrict__ logit_bias) {
   pdl_wait();
   extern __shared__ __align__(16) uint8_t sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -372,6 +373,13 @@ __global__ void __launch_bounds__(kRouteWarps * 32) k_route_topk(const float* __
   for (int j = 0; j < kRouteMaxE / 32; ++j) {
     const int i = lane + 32 * j;
     xr[j] = i < E ? row[i] : 0.f;
+  }
+  if (logit_bias) {  // an additive prior on the logits (fp32 add)
+#pragma unroll
+    for (int j = 0; j < kRouteMaxE / 32; ++j) {
+      const int i = lane + 32 * j;
+      if (i < E) xr[j] = __fadd_rn(xr[j], logit_bias[i]);
+    }
   }
 #pragma unroll
   for (int j = 0; j < kRouteMaxE / 32; ++j) {

@@ -19,6 +19,14 @@ from .. import config, moe
 from ..distributed import all_reduce, get_tp_rank, get_tp_size
 
 
+def rms_norm_gemma(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """Gemma-style RMS norm, the weight stored as an offset from 1.0 (``:59-62``), on the GPU
+    kernel: ``bf16(x * rsqrt(mean(x^2) + eps) * bf16(1 + weight))``."""
+    shape = x.shape
+    out = moe.add_rms_norm_gemma(x.reshape(-1, shape[-1]).contiguous(), weight.contiguous(), eps=eps)
+    return out.reshape(shape)
+
+
 def _fast_fp8_quantize(x: torch.Tensor, block_size: int = 128):
     """Per-token per-128-channel e4m3 quantisation (``:71-86``): ``(x_fp8 [M,K], x_scale [M,K/128])``."""
     assert block_size == 128, "only 128-channel blocks"
@@ -59,8 +67,10 @@ def _layout(weights: dict, num_experts: int, tp: int) -> str:
 
 
 def moe_forward(hidden: torch.Tensor, weights: dict, *, top_k: int | None = None,
-                return_routing: bool = False) -> torch.Tensor:
-    """MoE forward. hidden: [total, HIDDEN] bf16 -> output: [total, HIDDEN] bf16 (``:561-675``)."""
+                return_routing: bool = False, logit_bias: torch.Tensor | None = None) -> torch.Tensor:
+    """MoE forward. hidden: [total, HIDDEN] bf16 -> output: [total, HIDDEN] bf16 (``:561-675``).
+    ``logit_bias`` ([E] fp32, not in the reference) is added to the router logits: the expert
+    popularity prior of the 60-layer stack benchmark."""
     k = top_k if top_k is not None else config.NUM_EXPERTS_PER_TOK
     gate_w = weights["moe.gate.weight"]
     num_experts = gate_w.shape[0]
@@ -69,10 +79,11 @@ def moe_forward(hidden: torch.Tensor, weights: dict, *, top_k: int | None = None
     lay = _layout(weights, num_experts, tp)
     placement = 1 if (tp > 1 and lay == "expert") else 0
     if hidden.shape[1] % 64 == 0 and num_experts % 16 == 0 and 16 <= num_experts <= 1024:
-        topk_w, topk_ids = moe.router_from_hidden(hidden, gate_w, k)               # :567-572
+        topk_w, topk_ids = moe.router_from_hidden(hidden, gate_w, k, logit_bias=logit_bias)  # :567-572
         route = dict(topk_w=topk_w, topk_ids=topk_ids)
     else:
-        route = dict(router_logits=bf16_linear(hidden, gate_w).float())            # :568
+        logits = bf16_linear(hidden, gate_w).float()                                 # :568
+        route = dict(router_logits=logits if logit_bias is None else logits + logit_bias)
     res = moe.moe_layer(hidden, weights, top_k=k, num_experts=num_experts, placement=placement, tp=tp,
                         rank=rank, add_shared=(placement == 0 or rank == 0), return_routing=return_routing, **route)
     out = res[0] if return_routing else res

@@ -37,12 +37,15 @@ def route_topk(logits: torch.Tensor, k: int, renormalize: bool = True,
 
 def router_from_hidden(hidden: torch.Tensor, gate_weight: torch.Tensor, k: int, renormalize: bool = True,
                        round_logits_bf16: bool = True, w_dtype: torch.dtype = torch.bfloat16,
-                       ids_dtype: torch.dtype = torch.int32, return_logits: bool = False):
+                       ids_dtype: torch.dtype = torch.int32, return_logits: bool = False,
+                       logit_bias: torch.Tensor | None = None):
     """Router from the hidden states on the tensor cores: ``hidden @ gate_weight.T`` (bf16 in, fp32
     accumulation), optionally rounded to bf16 (``qwen35_layer_v2.py:567-568``), then softmax,
     top-k and renormalisation as :func:`route_topk` (``:569-572``).  With
     ``round_logits_bf16=False`` and fp32 weights it is ``moe_dispatch.moe_gate``
-    (``kernels/moe_dispatch.py:8-24``).  Returns ``(topk_w, topk_ids[, logits])``."""
+    (``kernels/moe_dispatch.py:8-24``).  ``logit_bias`` ([E] fp32, not in the reference) is added
+    to the logits before the softmax: the expert-popularity prior of the 60-layer stack
+    benchmark.  Returns ``(topk_w, topk_ids[, logits])``; ``logits`` exclude the bias."""
     lib = _lib.load()
     _cuda(hidden, "hidden")
     _cuda(gate_weight, "gate_weight")
@@ -58,10 +61,44 @@ def router_from_hidden(hidden: torch.Tensor, gate_weight: torch.Tensor, k: int, 
     if nbytes == 0:
         check(_lib.MSV_ERR_INVALID, "msv_router_workspace_size")
     ws = _lib.workspace(nbytes, hidden.device)
-    check(lib.msv_router_from_hidden(ptr(hidden), ptr(gate_weight), t, h, e, k, int(renormalize),
-                                     int(round_logits_bf16), ptr(w), _DT[w_dtype], ptr(ids), _DT[ids_dtype],
-                                     ptr(logits), ptr(ws), ws.numel(), stream_ptr()), "msv_router_from_hidden")
+    if logit_bias is None:
+        check(lib.msv_router_from_hidden(ptr(hidden), ptr(gate_weight), t, h, e, k, int(renormalize),
+                                         int(round_logits_bf16), ptr(w), _DT[w_dtype], ptr(ids), _DT[ids_dtype],
+                                         ptr(logits), ptr(ws), ws.numel(), stream_ptr()), "msv_router_from_hidden")
+    else:
+        _cuda(logit_bias, "logit_bias")
+        assert logit_bias.dtype == torch.float32 and logit_bias.shape == (e,) and logit_bias.is_contiguous()
+        check(lib.msv_router_from_hidden_bias(ptr(hidden), ptr(gate_weight), t, h, e, k, int(renormalize),
+                                              int(round_logits_bf16), ptr(logit_bias), ptr(w), _DT[w_dtype], ptr(ids),
+                                              _DT[ids_dtype], ptr(logits), ptr(ws), ws.numel(), stream_ptr()),
+              "msv_router_from_hidden_bias")
     return (w, ids, logits) if return_logits else (w, ids)
+
+
+def add_rms_norm_gemma(h: torch.Tensor, weight: torch.Tensor | None, add: torch.Tensor | None = None,
+                       eps: float = 1e-6, out: torch.Tensor | None = None, norm: bool = True):
+    """``rms_norm_gemma`` of ``qwen35_layer_v2.py:59-62`` as the decoder layer calls it
+    (``:713-715``), with the residual add before it fused in: when ``add`` is given, ``h`` is
+    first updated in place to ``bf16(h + add)``.  Returns the normalised ``[T, H]`` bf16 tensor
+    (``out`` when given), or ``h`` when ``norm`` is False (add only)."""
+    lib = _lib.load()
+    _cuda(h, "h")
+    assert h.dtype == torch.bfloat16 and h.dim() == 2 and h.is_contiguous()
+    t, hd = h.shape
+    if add is not None:
+        _cuda(add, "add")
+        assert add.dtype == torch.bfloat16 and add.shape == h.shape and add.is_contiguous()
+    if norm:
+        _cuda(weight, "weight")
+        assert weight.dtype == torch.bfloat16 and weight.shape == (hd,) and weight.is_contiguous()
+        if out is None:
+            out = torch.empty_like(h)
+    else:
+        assert add is not None, "add-only needs add"
+        out = None
+    check(lib.msv_add_rms_norm_gemma(ptr(h), ptr(add), ptr(weight) if norm else None, t, hd, float(eps), ptr(out),
+                                     stream_ptr()), "msv_add_rms_norm_gemma")
+    return out if norm else h
 
 
 def topk_select(values: torch.Tensor, k: int, ids_dtype: torch.dtype = torch.int64):
@@ -266,6 +303,11 @@ def moe_layer(hidden: torch.Tensor, weights: dict, top_k: int, num_experts: int,
 def ctypes_ref(obj):
     import ctypes
     return ctypes.byref(obj)
+
+
+def launch_count() -> int:
+    """Kernels this library has launched in this process (a graph replay does not count)."""
+    return int(_lib.load().msv_launch_count())
 
 
 def check_device_error() -> None:

@@ -126,6 +126,30 @@ def route(logits: torch.Tensor, k: int, weight_dtype=torch.bfloat16):
     return w.to(weight_dtype), ids
 
 
+def route_biased(logits: torch.Tensor, logit_bias: torch.Tensor, k: int, weight_dtype=torch.bfloat16):
+    """:func:`route` on ``logits + logit_bias`` (fp32 add): the 60-layer stack benchmark's
+    expert-popularity prior on top of the router logits (not a reference op)."""
+    return route(logits.float() + logit_bias.float(), k, weight_dtype)
+
+
+def rms_norm_gemma(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """Gemma-style RMS norm (``qwen35_layer_v2.py:59-62``): ``w = bf16(1 + float(weight))``,
+    then ``F.rms_norm`` on the bf16 input, which on the CPU computes in fp32 and rounds once."""
+    w = (1.0 + weight.float()).to(x.dtype)
+    return torch.nn.functional.rms_norm(x, (x.shape[-1],), w, eps).to(x.dtype)
+
+
+def moe_block(h: torch.Tensor, weights: dict, num_experts: int, k: int, logit_bias=None, eps: float = 1e-6):
+    """The MoE half of the decode layer (``qwen35_layer_v2.py:712-715``):
+    ``h + moe_forward(rms_norm_gemma(h, post_attention_layernorm.weight))``, with the router
+    logits from the bf16 gate GEMM (plus an optional prior) routed by :func:`route`."""
+    x2 = rms_norm_gemma(h, weights["post_attention_layernorm.weight"], eps)
+    logits = bf16_linear(x2, weights["moe.gate.weight"]).float()
+    if logit_bias is not None:
+        logits = logits + logit_bias.float()
+    return h + moe_forward(x2, weights, num_experts, k, logits=logits)
+
+
 def moe_gate(hidden: torch.Tensor, gate_weight: torch.Tensor, k: int):
     """Kernel-layer router with fp32 logits (``muserve/kernels/moe_dispatch.py:8-24``)."""
     logits = F.linear(hidden.float(), gate_weight.float())

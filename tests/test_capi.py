@@ -39,6 +39,10 @@ def test_version_and_error_string(lib):
     lambda lib: lib.msv_fp8_quant_128(None, 0, 4, 100, None, None, 0, None, 0, 0, None),
     lambda lib: lib.msv_ragged_moe_gemm_fp8(None, None, 4, 100, None, None, 2, 128, None, None, None, 0, None),
     lambda lib: lib.msv_gemm_fp8_nt_groupwise(None, None, 4, 128, None, None, 100, None, None, 0, None),
+    lambda lib: lib.msv_add_rms_norm_gemma(None, None, None, 4, 4096, 1e-6, None, None),
+    lambda lib: lib.msv_add_rms_norm_gemma(None, None, None, 4, 4100, 1e-6, None, None),
+    lambda lib: lib.msv_router_from_hidden_bias(None, None, 4, 4096, 512, 10, 1, 1, None, None, 1, None, 2, None,
+                                                None, 0, None),
 ])
 def test_bad_arguments_rejected(lib, call):
     assert call(lib) == L.MSV_ERR_INVALID
