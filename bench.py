@@ -271,8 +271,10 @@ def run_ours(args, world, rank, local):
         for _ in range(n_soak):
             step()
         t0.record(stream)
+        n_launch0 = moe.launch_count()
         for i in range(args.steps):
             step(i)
+        n_launches = moe.launch_count() - n_launch0
         t1.record(stream)
         torch.cuda.synchronize()
         clk.mark(False)
@@ -373,7 +375,7 @@ def run_ours(args, world, rank, local):
         "layer": {"hbm_gbs": layer_gbs, "hbm_frac": layer_gbs / hbm, "n_touched_experts": n_touched,
                   "fp8_tflops": flops / (ms_step / 1e3) / 1e12, "stage_ms": stage_ms,
                   "allreduce_ms": ar_ms, "allreduce_share": ar_ms / ms_step if tp > 1 else 0.0},
-        "gpu_launches": 6 * args.steps,
+        "gpu_launches": n_launches,
         "clocks": dict(clk.summary(), window=f"timed region + {n_soak} identical untimed steps just before it"),
         "e2e": e2e,
         "cpu_baseline": cpu,
