@@ -263,6 +263,66 @@ int msv_moe_forward_profiled(const msv_moe_shape* shape, const msv_moe_weights* 
                              const float* router_logits, void* topk_w, int32_t* topk_ids, void* out, int flags,
                              void* workspace, size_t workspace_bytes, msv_stream_t stream, void* const* events);
 
+/* ── tensor-parallel combine + all-reduce over NVLink peer memory ────────────────────── */
+
+/*
+ * CUDA IPC of one device allocation between the ranks' processes (one process per GPU).
+ * msv_ipc_export: a handle (msv_ipc_handle_bytes() bytes) for the allocation that holds `ptr`,
+ * and ptr's offset in it.  msv_ipc_import: another process's handle + offset -> a pointer
+ * valid in this process (peer loads and stores over NVLink).  msv_ipc_close: unmap a pointer
+ * msv_ipc_import returned.  (Set-up of msv_moe_forward_tp; no reference counterpart.)
+ */
+size_t msv_ipc_handle_bytes(void);
+int msv_ipc_export(const void* ptr, void* handle_out, uint64_t* offset_out);
+int msv_ipc_import(const void* handle, uint64_t offset, void** ptr_out);
+int msv_ipc_close(void* ptr);
+
+#define MSV_MAX_TP 8
+
+/*
+ * The TP group of msv_moe_forward_tp.  Every rank allocates one shared buffer of
+ * msv_tp_shared_bytes(max_tokens, hidden) bytes (256-byte aligned, zero-filled: it holds the
+ * flags) and one epoch buffer of msv_tp_epoch_bytes() bytes (zero-filled), exports the shared
+ * buffer and imports every other rank's.  shared[p] is rank p's buffer as mapped in this
+ * process (shared[rank] is the local one).  After a MSV_ERR_TIMEOUT the buffers must be
+ * zero-filled again on every rank before the next call.
+ */
+typedef struct msv_tp_comm {
+  int world;                     /* ranks in the group, 1..MSV_MAX_TP */
+  int rank;                      /* this rank */
+  int max_tokens;                /* tokens each shared buffer holds */
+  int hidden;                    /* H the shared buffers were sized for */
+  void* shared[MSV_MAX_TP];
+  unsigned int* epoch;
+} msv_tp_comm;
+
+size_t msv_tp_shared_bytes(int max_tokens, int hidden);
+size_t msv_tp_epoch_bytes(void);
+
+/*
+ * msv_moe_forward with the weighted combine fused with the sum over the TP group: every rank
+ * passes its shard of the layer (shape.inter = I/tp with placement 0, or placement 1), and
+ * `out` receives the all-reduced [T,H] bf16 result, identical on every rank.
+ *   replaces: muserve/model/qwen35_layer_v2.py:657-662 with muserve/distributed.py:62-64
+ *             (the per-rank result, then all_reduce(SUM) over the TP group)
+ * The partials are summed in fp32 in rank order and rounded to bf16 once.  One persistent CTA
+ * per SM (at most T) combines its tokens, exchanges flags with the same CTA on every rank
+ * (bounded waits: MSV_ERR_TIMEOUT through msv_check_device_error), sums its H/world-column
+ * slice over the ranks' partials (peer loads), writes it to every rank (peer stores), and
+ * after a second flag exchange copies its rows to `out`.  T <= comm->max_tokens,
+ * H == comm->hidden, H % (8 * world) == 0.  Every rank must make the same calls in the same
+ * order on the same number of SMs.
+ */
+int msv_moe_forward_tp(const msv_moe_shape* shape, const msv_moe_weights* weights, const void* hidden,
+                       const float* router_logits, void* topk_w, int32_t* topk_ids, void* out, int flags,
+                       void* workspace, size_t workspace_bytes, const msv_tp_comm* comm, msv_stream_t stream);
+/* msv_moe_forward_tp with the 7 events of msv_moe_forward_profiled (the last stage is the
+   fused combine + all-reduce). */
+int msv_moe_forward_tp_profiled(const msv_moe_shape* shape, const msv_moe_weights* weights, const void* hidden,
+                                const float* router_logits, void* topk_w, int32_t* topk_ids, void* out, int flags,
+                                void* workspace, size_t workspace_bytes, const msv_tp_comm* comm,
+                                msv_stream_t stream, void* const* events);
+
 /*
  * Reads and clears the device error word that the layer's kernels raise when a bounded wait
  * gives up.  Synchronises `stream`.  Returns MSV_OK or MSV_ERR_TIMEOUT.

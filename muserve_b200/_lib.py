@@ -38,6 +38,13 @@ class MoeWeights(ctypes.Structure):
                 ("sh_down_s", P), ("sh_gate_logit_w", P)]
 
 
+MAX_TP = 8
+
+
+class TpComm(ctypes.Structure):
+    _fields_ = [("world", I), ("rank", I), ("max_tokens", I), ("hidden", I), ("shared", P * MAX_TP), ("epoch", P)]
+
+
 _SIGS = {
     "msv_last_error": (ctypes.c_char_p, []),
     "msv_version": (I, []),
@@ -60,6 +67,16 @@ _SIGS = {
     "msv_moe_forward": (I, [ctypes.POINTER(MoeShape), ctypes.POINTER(MoeWeights), P, P, P, P, P, I, P, SZ, P]),
     "msv_moe_forward_profiled": (I, [ctypes.POINTER(MoeShape), ctypes.POINTER(MoeWeights), P, P, P, P, P, I, P, SZ,
                                      P, P]),
+    "msv_ipc_handle_bytes": (SZ, []),
+    "msv_ipc_export": (I, [P, P, ctypes.POINTER(ctypes.c_uint64)]),
+    "msv_ipc_import": (I, [P, ctypes.c_uint64, ctypes.POINTER(P)]),
+    "msv_ipc_close": (I, [P]),
+    "msv_tp_shared_bytes": (SZ, [I, I]),
+    "msv_tp_epoch_bytes": (SZ, []),
+    "msv_moe_forward_tp": (I, [ctypes.POINTER(MoeShape), ctypes.POINTER(MoeWeights), P, P, P, P, P, I, P, SZ,
+                               ctypes.POINTER(TpComm), P]),
+    "msv_moe_forward_tp_profiled": (I, [ctypes.POINTER(MoeShape), ctypes.POINTER(MoeWeights), P, P, P, P, P, I, P,
+                                        SZ, ctypes.POINTER(TpComm), P, P]),
 }
 
 _lock = threading.Lock()

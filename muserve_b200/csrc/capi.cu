@@ -8,6 +8,7 @@
 #include <string>
 #include <unordered_map>
 
+#include "combine_ar.cuh"
 #include "common.cuh"
 #include "grouped_gemm.cuh"
 #include "grouped_gemm_rows.cuh"
@@ -86,6 +87,30 @@ EncodeTiledFn encode_fn() {
       fn = reinterpret_cast<EncodeTiledFn>(p);
   });
   return fn;
+}
+
+using AddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+AddressRangeFn address_range_fn() {
+  static AddressRangeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<AddressRangeFn>(p);
+  });
+  return fn;
+}
+
+// pointers msv_ipc_import returned -> the mapped allocation's base (for msv_ipc_close)
+std::mutex g_ipc_mu;
+std::unordered_map<uintptr_t, void*> g_ipc_bases;
+
+// one rank's shared buffer: partial rows, gathered rows, flags
+size_t tp_rows_bytes(int max_tokens, int hidden) {
+  return (((size_t)max_tokens * (size_t)hidden * 2) + 255) & ~(size_t)255;
 }
 
 struct MapKey {
@@ -829,7 +854,7 @@ size_t msv_moe_forward_workspace_size(const msv_moe_shape* shape) {
 namespace {
 int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const void* hidden, const float* logits,
                      void* topk_w, int32_t* topk_ids, void* out, int flags, void* workspace, size_t ws_bytes,
-                     cudaStream_t stream, cudaEvent_t* ev) {
+                     cudaStream_t stream, cudaEvent_t* ev, const msv_tp_comm* comm = nullptr) {
   auto mark = [&](int i) -> int {
     return (ev && ev[i]) ? cuda_check(cudaEventRecord(ev[i], stream), "cudaEventRecord") : (int)MSV_OK;
   };
@@ -1125,9 +1150,49 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
   cb.gate_val = (do_shared && W->sh_gate_logit_w) ? w.gate_val : nullptr;
   cb.out = static_cast<__nv_bfloat16*>(out);
   cb.ld_out = L.H;
+  if (comm) {
+    // combine fused with the sum over the TP group (peer memory; a group of one exchanges
+    // flags with itself)
+    CombineArArgs ar{};
+    ar.c = cb;
+    const size_t rb = tp_rows_bytes(comm->max_tokens, comm->hidden);
+    for (int p = 0; p < comm->world; ++p) {
+      uint8_t* base = static_cast<uint8_t*>(comm->shared[p]);
+      ar.part[p] = reinterpret_cast<__nv_bfloat16*>(base);
+      ar.gath[p] = reinterpret_cast<__nv_bfloat16*>(base + rb);
+      ar.flags[p] = reinterpret_cast<unsigned int*>(base + 2 * rb);
+    }
+    ar.epoch = comm->epoch;
+    ar.world = comm->world;
+    ar.rank = comm->rank;
+    ar.err = d->err_word;
+    int g = L.T < d->num_sms ? L.T : d->num_sms;
+    g = g < kArMaxCtas ? g : kArMaxCtas;
+    const dim3 grid(g), block(combine_threads(L.H));
+    if (cb.mode == MSV_COMBINE_V2) launch_k(k_combine_ar<MSV_COMBINE_V2>, grid, block, 0, stream, ar);
+    else if (cb.mode == MSV_COMBINE_DISPATCH) launch_k(k_combine_ar<MSV_COMBINE_DISPATCH>, grid, block, 0, stream, ar);
+    else launch_k(k_combine_ar<MSV_COMBINE_BATCHED>, grid, block, 0, stream, ar);
+    if (int rc = cuda_check(cudaGetLastError(), "launch combine_ar")) return rc;
+    return mark(6);
+  }
   launch_combine(cb, stream);
   if (int rc = cuda_check(cudaGetLastError(), "launch combine")) return rc;
   return mark(6);
+}
+
+int check_tp_comm(const msv_tp_comm* c, const msv_moe_shape* s) {
+  if (!c) return fail(MSV_ERR_INVALID, "msv_moe_forward_tp: null comm");
+  if (c->world < 1 || c->world > MSV_MAX_TP || c->rank < 0 || c->rank >= c->world || !c->epoch)
+    return fail(MSV_ERR_INVALID, "msv_moe_forward_tp: bad group (world=%d rank=%d)", c->world, c->rank);
+  if (!s || s->tokens > c->max_tokens || s->hidden != c->hidden || s->hidden % (8 * c->world))
+    return fail(MSV_ERR_INVALID,
+                "msv_moe_forward_tp: T=%d must be <= max_tokens=%d, H=%d == hidden=%d and a multiple of 8*world",
+                s ? s->tokens : -1, c->max_tokens, s ? s->hidden : -1, c->hidden);
+  for (int p = 0; p < c->world; ++p)
+    if (!c->shared[p] || !is_pow2_aligned(c->shared[p], 256))
+      return fail(MSV_ERR_INVALID, "msv_moe_forward_tp: shared[%d] null or not 256-byte aligned", p);
+  if (!is_pow2_aligned(c->epoch, 16)) return fail(MSV_ERR_INVALID, "msv_moe_forward_tp: epoch not 16-byte aligned");
+  return MSV_OK;
 }
 }  // namespace
 
@@ -1144,6 +1209,77 @@ int msv_moe_forward_profiled(const msv_moe_shape* s, const msv_moe_weights* W, c
   cudaEvent_t ev[7];
   for (int i = 0; i < 7; ++i) ev[i] = static_cast<cudaEvent_t>(events[i]);
   return moe_forward_impl(s, W, hidden, logits, topk_w, topk_ids, out, flags, workspace, ws_bytes, stream, ev);
+}
+
+size_t msv_ipc_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+int msv_ipc_export(const void* ptr, void* handle_out, uint64_t* offset_out) {
+  if (!ptr || !handle_out || !offset_out) return fail(MSV_ERR_INVALID, "msv_ipc_export: null argument");
+  AddressRangeFn fn = address_range_fn();
+  if (!fn) return fail(MSV_ERR_CUDA, "cuMemGetAddressRange unavailable from the driver");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (fn(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return fail(MSV_ERR_INVALID, "msv_ipc_export: not a device allocation");
+  cudaIpcMemHandle_t h;
+  if (int rc = cuda_check(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)), "cudaIpcGetMemHandle")) return rc;
+  std::memcpy(handle_out, &h, sizeof h);
+  *offset_out = static_cast<uint64_t>(reinterpret_cast<uintptr_t>(ptr) - static_cast<uintptr_t>(base));
+  return MSV_OK;
+}
+
+int msv_ipc_import(const void* handle, uint64_t offset, void** ptr_out) {
+  if (!handle || !ptr_out) return fail(MSV_ERR_INVALID, "msv_ipc_import: null argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof h);
+  void* base = nullptr;
+  if (int rc = cuda_check(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle"))
+    return rc;
+  void* p = static_cast<uint8_t*>(base) + offset;
+  {
+    std::lock_guard<std::mutex> g(g_ipc_mu);
+    g_ipc_bases[reinterpret_cast<uintptr_t>(p)] = base;
+  }
+  *ptr_out = p;
+  return MSV_OK;
+}
+
+int msv_ipc_close(void* ptr) {
+  void* base = nullptr;
+  {
+    std::lock_guard<std::mutex> g(g_ipc_mu);
+    auto it = g_ipc_bases.find(reinterpret_cast<uintptr_t>(ptr));
+    if (it == g_ipc_bases.end()) return fail(MSV_ERR_INVALID, "msv_ipc_close: not a pointer msv_ipc_import returned");
+    base = it->second;
+    g_ipc_bases.erase(it);
+  }
+  return cuda_check(cudaIpcCloseMemHandle(base), "cudaIpcCloseMemHandle");
+}
+
+size_t msv_tp_shared_bytes(int max_tokens, int hidden) {
+  if (max_tokens <= 0 || hidden <= 0) return 0;
+  return 2 * tp_rows_bytes(max_tokens, hidden) + (size_t)2 * kMaxTpRanks * kArMaxCtas * sizeof(unsigned int);
+}
+
+size_t msv_tp_epoch_bytes(void) { return (size_t)kArMaxCtas * sizeof(unsigned int); }
+
+int msv_moe_forward_tp(const msv_moe_shape* s, const msv_moe_weights* W, const void* hidden, const float* logits,
+                       void* topk_w, int32_t* topk_ids, void* out, int flags, void* workspace, size_t ws_bytes,
+                       const msv_tp_comm* comm, msv_stream_t stream) {
+  if (int rc = check_tp_comm(comm, s)) return rc;
+  return moe_forward_impl(s, W, hidden, logits, topk_w, topk_ids, out, flags, workspace, ws_bytes, stream, nullptr,
+                          comm);
+}
+
+int msv_moe_forward_tp_profiled(const msv_moe_shape* s, const msv_moe_weights* W, const void* hidden,
+                                const float* logits, void* topk_w, int32_t* topk_ids, void* out, int flags,
+                                void* workspace, size_t ws_bytes, const msv_tp_comm* comm, msv_stream_t stream,
+                                void* const* events) {
+  if (!events) return fail(MSV_ERR_INVALID, "msv_moe_forward_tp_profiled: null events");
+  if (int rc = check_tp_comm(comm, s)) return rc;
+  cudaEvent_t ev[7];
+  for (int i = 0; i < 7; ++i) ev[i] = static_cast<cudaEvent_t>(events[i]);
+  return moe_forward_impl(s, W, hidden, logits, topk_w, topk_ids, out, flags, workspace, ws_bytes, stream, ev, comm);
 }
 
 }  // extern "C"

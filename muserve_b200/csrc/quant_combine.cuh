@@ -213,16 +213,13 @@ inline int combine_threads(int H) {
   return t < kCombineThreads ? t : kCombineThreads;
 }
 
-// One CTA per token; each thread produces 8 consecutive channels per pass (one pass when
-// H <= 4096).  Warp 0 reads the token's k slots in parallel (and orders them by expert id for
-// the per-expert modes); the channel loop loads 8 slot rows before it sums them (two CTAs
-// per SM keep enough rows in flight at large batches).
+// One token's combined row into dst, by the whole CTA (s_row / s_w: the CTA's shared slots).
+// Each thread produces 8 consecutive channels per pass (one pass when H <= 4096).  Warp 0
+// reads the token's k slots in parallel (and orders them by expert id for the per-expert
+// modes); the channel loop loads 8 slot rows before it sums them.
 template <int MODE>
-__global__ void __launch_bounds__(kCombineThreads, 2) k_combine(CombineArgs a) {
-  pdl_wait();
-  const int t = blockIdx.x;
-  __shared__ int s_row[16];
-  __shared__ float s_w[16];
+MSV_DEVICE void combine_token(const CombineArgs& a, int t, int* s_row, float* s_w, __nv_bfloat16* dst) {
+  __syncthreads();  // the previous token's slots are no longer read
   if (threadIdx.x < 32) {
     const int j = threadIdx.x;
     int r = -1, id = 0x7fffffff;
@@ -297,8 +294,18 @@ __global__ void __launch_bounds__(kCombineThreads, 2) k_combine(CombineArgs a) {
       const __nv_bfloat162 p = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
       ow[i] = *reinterpret_cast<const uint32_t*>(&p);
     }
-    *reinterpret_cast<uint4*>(a.out + (int64_t)t * a.ld_out + c) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+    *reinterpret_cast<uint4*>(dst + c) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
   }
+}
+
+// One CTA per token (two CTAs per SM keep enough rows in flight at large batches).
+template <int MODE>
+__global__ void __launch_bounds__(kCombineThreads, 2) k_combine(CombineArgs a) {
+  pdl_wait();
+  __shared__ int s_row[16];
+  __shared__ float s_w[16];
+  const int t = blockIdx.x;
+  combine_token<MODE>(a, t, s_row, s_w, a.out + (int64_t)t * a.ld_out);
   pdl_trigger();
 }
 

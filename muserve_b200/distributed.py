@@ -39,6 +39,7 @@ def init_distributed(backend: str | None = None, timeout_s: float = 120.0) -> No
 
 def destroy_distributed() -> None:
     global _TP_GROUP, _CPU_GROUP, _TP_RANK, _TP_SIZE
+    close_fused_allreduce()
     if dist.is_initialized():
         dist.destroy_process_group()
     _TP_GROUP, _CPU_GROUP, _TP_RANK, _TP_SIZE = None, None, 0, 1
@@ -70,3 +71,87 @@ def all_gather_into_tensor(output: torch.Tensor, input: torch.Tensor) -> None:
 def barrier() -> None:
     if dist.is_initialized():
         dist.barrier(group=get_tp_group())
+
+
+class TpComm:
+    """Peer-memory buffers of the TP group for the fused combine + all-reduce
+    (``msv_moe_forward_tp``).  Every rank allocates one shared buffer (partial rows, gathered
+    rows, flags) and one epoch buffer, exports the shared buffer by CUDA IPC, and maps every
+    other rank's (handles exchanged over the CPU group).  Collective: all ranks construct and
+    close it together."""
+
+    def __init__(self, max_tokens: int, hidden: int, device: torch.device | None = None):
+        import ctypes
+
+        from . import _lib
+        lib = _lib.load()
+        self.lib = lib
+        self.world, self.rank = get_tp_size(), get_tp_rank()
+        if self.world > _lib.MAX_TP:
+            raise ValueError(f"the fused all-reduce supports at most {_lib.MAX_TP} ranks")
+        if hidden % (8 * self.world):
+            raise ValueError("hidden must be a multiple of 8 * world")
+        dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.max_tokens, self.hidden = max_tokens, hidden
+        self.buf = torch.zeros(lib.msv_tp_shared_bytes(max_tokens, hidden), dtype=torch.uint8, device=dev)
+        self.epoch = torch.zeros(lib.msv_tp_epoch_bytes() // 4, dtype=torch.int32, device=dev)
+        hb = lib.msv_ipc_handle_bytes()
+        handle = (ctypes.c_char * hb)()
+        off = ctypes.c_uint64(0)
+        _lib.check(lib.msv_ipc_export(self.buf.data_ptr(), handle, ctypes.byref(off)), "msv_ipc_export")
+        mine = (bytes(handle), int(off.value))
+        allh = [None] * self.world
+        if self.world > 1:
+            dist.all_gather_object(allh, mine, group=_CPU_GROUP)
+        else:
+            allh = [mine]
+        self.imported = []
+        ptrs = []
+        for p, (h, o) in enumerate(allh):
+            if p == self.rank:
+                ptrs.append(self.buf.data_ptr())
+                continue
+            out = ctypes.c_void_p()
+            hbuf = (ctypes.c_char * hb).from_buffer_copy(h)
+            _lib.check(lib.msv_ipc_import(hbuf, ctypes.c_uint64(o), ctypes.byref(out)), "msv_ipc_import")
+            self.imported.append(out.value)
+            ptrs.append(out.value)
+        shared = (ctypes.c_void_p * _lib.MAX_TP)(*(ptrs + [None] * (_lib.MAX_TP - len(ptrs))))
+        self.struct = _lib.TpComm(world=self.world, rank=self.rank, max_tokens=max_tokens, hidden=hidden,
+                                  shared=shared, epoch=self.epoch.data_ptr())
+        torch.cuda.synchronize(dev)
+        barrier()  # every rank's flags are zero before any rank's first call
+
+    def close(self) -> None:
+        torch.cuda.synchronize()
+        barrier()  # no rank still reads or writes another's buffer
+        for p in self.imported:
+            self.lib.msv_ipc_close(p)
+        self.imported = []
+
+
+_FUSED: TpComm | None = None
+
+
+def init_fused_allreduce(max_tokens: int, hidden: int) -> TpComm:
+    """Enable the fused combine + all-reduce for layers of up to ``max_tokens`` tokens of width
+    ``hidden`` (collective).  ``model.qwen35_layer_v2.moe_forward`` then skips ``all_reduce``."""
+    global _FUSED
+    close_fused_allreduce()
+    _FUSED = TpComm(max_tokens, hidden)
+    return _FUSED
+
+
+def fused_allreduce_comm(tokens: int, hidden: int) -> TpComm | None:
+    """The group's fused all-reduce buffers when they fit a [tokens, hidden] layer, else None."""
+    c = _FUSED
+    if c is None or get_tp_size() <= 1 or tokens > c.max_tokens or hidden != c.hidden:
+        return None
+    return c
+
+
+def close_fused_allreduce() -> None:
+    global _FUSED
+    if _FUSED is not None:
+        _FUSED.close()
+        _FUSED = None

@@ -16,7 +16,7 @@ import torch
 import torch.nn.functional as F
 
 from .. import config, moe
-from ..distributed import all_reduce, get_tp_rank, get_tp_size
+from ..distributed import all_reduce, fused_allreduce_comm, get_tp_rank, get_tp_size
 
 
 def rms_norm_gemma(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
@@ -84,9 +84,12 @@ def moe_forward(hidden: torch.Tensor, weights: dict, *, top_k: int | None = None
     else:
         logits = bf16_linear(hidden, gate_w).float()                                 # :568
         route = dict(router_logits=logits if logit_bias is None else logits + logit_bias)
+    # with the group's fused buffers the combine sums over the TP group itself (peer memory)
+    comm = fused_allreduce_comm(hidden.shape[0], hidden.shape[1]) if tp > 1 else None
     res = moe.moe_layer(hidden, weights, top_k=k, num_experts=num_experts, placement=placement, tp=tp,
-                        rank=rank, add_shared=(placement == 0 or rank == 0), return_routing=return_routing, **route)
+                        rank=rank, add_shared=(placement == 0 or rank == 0), return_routing=return_routing,
+                        comm=comm, **route)
     out = res[0] if return_routing else res
-    if tp > 1:
+    if tp > 1 and comm is None:
         all_reduce(out)
     return res if return_routing else out

@@ -262,11 +262,13 @@ def moe_layer(hidden: torch.Tensor, weights: dict, top_k: int, num_experts: int,
               topk_ids: torch.Tensor | None = None, placement: int = 0, tp: int = 1, rank: int = 0,
               add_shared: bool = True, combine_mode: int = _lib.COMBINE_V2,
               weights_dtype: torch.dtype = torch.bfloat16, out: torch.Tensor | None = None,
-              return_routing: bool = False):
+              return_routing: bool = False, comm=None):
     """One MoE layer (``qwen35_layer_v2.py:561-675`` after the router GEMM) in six kernels:
     router, dispatch bookkeeping, gather+quantise, gate_up GEMM (SwiGLU + requant epilogue),
     down GEMM, weighted combine (+ shared expert).  Either ``router_logits`` or
-    ``topk_w``/``topk_ids`` (given routing) must be passed."""
+    ``topk_w``/``topk_ids`` (given routing) must be passed.  With ``comm`` (a
+    :class:`muserve_b200.distributed.TpComm`) the combine is fused with the sum over the TP
+    group (``:657-662`` with ``distributed.py:62-64``) and ``out`` is the all-reduced result."""
     lib = _lib.load()
     assert hidden.dtype == torch.bfloat16 and hidden.dim() == 2 and hidden.is_contiguous()
     t, h = hidden.shape
@@ -292,9 +294,14 @@ def moe_layer(hidden: torch.Tensor, weights: dict, top_k: int, num_experts: int,
     if nbytes == 0:
         check(_lib.MSV_ERR_INVALID, "msv_moe_forward_workspace_size")
     ws = _lib.workspace(nbytes, hidden.device)
-    check(lib.msv_moe_forward(ctypes_ref(shape), ctypes_ref(ws_struct), ptr(hidden), ptr(router_logits),
-                              ptr(topk_w), ptr(topk_ids), ptr(out), flags, ptr(ws), ws.numel(), stream_ptr()),
-          "msv_moe_forward")
+    if comm is None:
+        check(lib.msv_moe_forward(ctypes_ref(shape), ctypes_ref(ws_struct), ptr(hidden), ptr(router_logits),
+                                  ptr(topk_w), ptr(topk_ids), ptr(out), flags, ptr(ws), ws.numel(), stream_ptr()),
+              "msv_moe_forward")
+    else:
+        check(lib.msv_moe_forward_tp(ctypes_ref(shape), ctypes_ref(ws_struct), ptr(hidden), ptr(router_logits),
+                                     ptr(topk_w), ptr(topk_ids), ptr(out), flags, ptr(ws), ws.numel(),
+                                     ctypes_ref(comm.struct), stream_ptr()), "msv_moe_forward_tp")
     if return_routing:
         return out, topk_w, topk_ids
     return out

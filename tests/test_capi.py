@@ -40,6 +40,9 @@ def test_version_and_error_string(lib):
     lambda lib: lib.msv_ragged_moe_gemm_fp8(None, None, 4, 100, None, None, 2, 128, None, None, None, 0, None),
     lambda lib: lib.msv_gemm_fp8_nt_groupwise(None, None, 4, 128, None, None, 100, None, None, 0, None),
     lambda lib: lib.msv_add_rms_norm_gemma(None, None, None, 4, 4096, 1e-6, None, None),
+    lambda lib: lib.msv_moe_forward_tp(None, None, None, None, None, None, None, 0, None, 0, None, None),
+    lambda lib: lib.msv_ipc_export(None, None, None),
+    lambda lib: lib.msv_ipc_import(None, 0, None),
     lambda lib: lib.msv_add_rms_norm_gemma(None, None, None, 4, 4100, 1e-6, None, None),
     lambda lib: lib.msv_router_from_hidden_bias(None, None, 4, 4096, 512, 10, 1, 1, None, None, 1, None, 2, None,
                                                 None, 0, None),
@@ -59,6 +62,11 @@ def test_workspace_sizes(lib):
     s.hidden, s.shared_inter = 4096, 512  # shared intermediate must equal routed
     assert lib.msv_moe_forward_workspace_size(ctypes.byref(s)) == 0
     assert lib.msv_ragged_gemm_workspace_size(1024, 2048) > 0
+    # fused TP combine: partial + gathered rows (256-byte aligned) + 2 x 8 x 1024 flags
+    assert lib.msv_tp_shared_bytes(256, 4096) == 2 * 256 * 4096 * 2 + 2 * 8 * 1024 * 4
+    assert lib.msv_tp_shared_bytes(0, 4096) == 0
+    assert lib.msv_tp_epoch_bytes() == 1024 * 4
+    assert lib.msv_ipc_handle_bytes() == 64
     assert lib.msv_gemm_fp8_workspace_size(64, 1024) > 0
 
 

@@ -1,0 +1,157 @@
+"""Weighted combine fused with the TP all-reduce over NVLink peer memory
+(qwen35_layer_v2.py:657-662 with distributed.py:62-64).
+
+On one GPU a group of one runs the same fused kernel (its flag exchange is with itself) and
+must equal the plain combine bit for bit, call after call and inside a CUDA graph.  With two
+or more GPUs, child processes (one per GPU) run the intermediate-sharded layer through the
+fused path and through NCCL: at two ranks both sum two bf16 partials in fp32 with one
+rounding, so the outputs are identical; every rank holds the same bits; and the result matches
+the unsharded oracle within the path's tolerance."""
+import os
+import socket
+
+import pytest
+import torch
+
+from conftest import assert_close_bf16
+from muserve_b200 import moe
+from oracle import moe_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+
+def _layer(cuda, h=1024, e=64, inter=512, seed=3):
+    w = orc.make_layer_weights(h, e, inter, inter, seed=seed)
+    return {k: v.to(cuda) for k, v in w.items() if torch.is_tensor(v)}
+
+
+def _group_of_one(cuda, max_tokens, hidden):
+    """A TpComm of one rank without a process group."""
+    import ctypes
+
+    from muserve_b200 import _lib
+    lib = _lib.load()
+
+    class One:
+        pass
+    c = One()
+    c.buf = torch.zeros(lib.msv_tp_shared_bytes(max_tokens, hidden), dtype=torch.uint8, device=cuda)
+    c.epoch = torch.zeros(lib.msv_tp_epoch_bytes() // 4, dtype=torch.int32, device=cuda)
+    shared = (ctypes.c_void_p * _lib.MAX_TP)(c.buf.data_ptr())
+    c.struct = _lib.TpComm(world=1, rank=0, max_tokens=max_tokens, hidden=hidden, shared=shared,
+                           epoch=c.epoch.data_ptr())
+    return c
+
+
+@pytest.mark.parametrize("T", [1, 37, 300])
+@pytest.mark.parametrize("mode", [0, 1, 2])
+def test_fused_group_of_one_equals_combine(cuda, T, mode):
+    w = _layer(cuda)
+    x = orc.make_hidden(T, 1024, 5).to(cuda)
+    lg = orc.make_hidden(T, 64, 6).float().to(cuda)
+    comm = _group_of_one(cuda, 512, 1024)
+    ref = moe.moe_layer(x, w, top_k=6, num_experts=64, router_logits=lg, combine_mode=mode)
+    for _ in range(3):  # the epochs advance call after call
+        got = moe.moe_layer(x, w, top_k=6, num_experts=64, router_logits=lg, combine_mode=mode, comm=comm)
+        assert torch.equal(got, ref)
+    moe.check_device_error()
+
+
+def test_fused_group_of_one_in_a_graph(cuda):
+    w = _layer(cuda)
+    x = orc.make_hidden(64, 1024, 7).to(cuda)
+    lg = orc.make_hidden(64, 64, 8).float().to(cuda)
+    comm = _group_of_one(cuda, 64, 1024)
+    ref = moe.moe_layer(x, w, top_k=6, num_experts=64, router_logits=lg)
+    out = torch.empty_like(ref)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            moe.moe_layer(x, w, top_k=6, num_experts=64, router_logits=lg, comm=comm, out=out)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        moe.moe_layer(x, w, top_k=6, num_experts=64, router_logits=lg, comm=comm, out=out)
+    for _ in range(4):
+        out.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
+    moe.check_device_error()
+    g.reset()
+
+
+def test_fused_rejects_bad_groups(cuda):
+    w = _layer(cuda)
+    x = orc.make_hidden(70, 1024, 9).to(cuda)
+    lg = orc.make_hidden(70, 64, 10).float().to(cuda)
+    comm = _group_of_one(cuda, 64, 1024)  # too few rows for 70 tokens
+    with pytest.raises(AssertionError):
+        moe.moe_layer(x, w, top_k=6, num_experts=64, router_logits=lg, comm=comm)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, T, result_dir):
+    os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
+                      MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+
+    from muserve_b200 import distributed as D
+    from muserve_b200.loader import shard_moe_weights
+    from muserve_b200.model import qwen35_layer_v2 as v2
+    D.init_distributed(backend="nccl", timeout_s=60)
+    dev = torch.device("cuda", rank)
+    full = orc.make_layer_weights(1024, 64, 512, 512, seed=11)
+    x = orc.make_hidden(T, 1024, 12)
+    lg = orc.make_hidden(T, 64, 13).float()
+    shard = {k: v.to(dev) for k, v in shard_moe_weights(full, world, rank, "inter").items() if torch.is_tensor(v)}
+    xd, lgd = x.to(dev), lg.to(dev)
+    # NCCL: this rank's partial, then the all-reduce
+    nccl = moe.moe_layer(xd, shard, top_k=6, num_experts=64, router_logits=lgd)
+    dist.all_reduce(nccl)
+    nccl_v2 = v2.moe_forward(xd, shard, top_k=6)
+    comm = D.init_fused_allreduce(512, 1024)
+    fused = [moe.moe_layer(xd, shard, top_k=6, num_experts=64, router_logits=lgd, comm=comm).clone()
+             for _ in range(3)]
+    fused_v2 = v2.moe_forward(xd, shard, top_k=6)  # the drop-in path picks the fused buffers up
+    torch.cuda.synchronize()
+    moe.check_device_error()
+    torch.save({"nccl": nccl.cpu(), "fused": [f.cpu() for f in fused], "nccl_v2": nccl_v2.cpu(),
+                "fused_v2": fused_v2.cpu()}, os.path.join(result_dir, f"r{rank}.pt"))
+    D.destroy_distributed()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("T", [5, 256])
+def test_fused_allreduce_two_ranks(cuda, tmp_path, T):
+    import torch.multiprocessing as mp
+    world = 2
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, T, str(tmp_path))) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            p.join()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    res = [torch.load(tmp_path / f"r{r}.pt") for r in range(world)]
+    for r in range(world):
+        for f in res[r]["fused"]:
+            assert torch.equal(f, res[0]["fused"][0])       # every rank, every call: the same bits
+        assert torch.equal(res[r]["fused"][0], res[r]["nccl"])  # two ranks: equal to NCCL's sum
+        assert torch.equal(res[r]["fused_v2"], res[r]["nccl_v2"])
+    full = orc.make_layer_weights(1024, 64, 512, 512, seed=11)
+    x = orc.make_hidden(T, 1024, 12)
+    lg = orc.make_hidden(T, 64, 13).float()
+    ref = orc.moe_forward(x, full, 64, 6, logits=lg)
+    assert_close_bf16(res[0]["fused"][0].float(), ref.float())
