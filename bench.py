@@ -7,7 +7,8 @@ N = 1  -> BASELINE config 1: full-shape decode layer (H=4096, 512 experts top-10
           expert, I=1024) on 64 tokens with uniform random router logits.
 N > 1  -> BASELINE config 3 (launched by torchrun, one rank per GPU): the same layer at TP=N
           with the expert intermediate sharded (column-parallel gate_up, row-parallel down),
-          256 tokens, per-rank partial [256,4096] bf16 summed by one NCCL all-reduce.
+          256 tokens; the per-rank [256,4096] bf16 partials are summed by the combine kernel itself
+          over NVLink peer memory (--nccl-allreduce: plain combine + one NCCL all-reduce).
 --workload prefill -> BASELINE config 2 on one GPU (8192 tokens, router GEMM on cuBLAS).
 --workload stack   -> BASELINE config 4: the 60-layer MoE decode stack (128 tokens, Zipf(1.2)
           logit prior, RMSNorm + router GEMM + layer per layer) as one CUDA graph at TP=N.
@@ -225,17 +226,34 @@ def run_ours(args, world, rank, local):
             e.record(stream)
     ev_arrays_p = [(ctypes.c_void_p * nst)(*[e.cuda_event for e in row]) for row in evs_p]
 
+    # TP: the combine fused with the all-reduce over NVLink peer memory (--nccl-allreduce: the
+    # plain combine, then NCCL's all-reduce)
+    comm = None
+    if tp > 1 and not args.nccl_allreduce:
+        from muserve_b200 import distributed as D
+        comm = D.init_fused_allreduce(tokens, H)
+    cref = ctypes.byref(comm.struct) if comm is not None else None
+
     def step(i=None, prof=False):
         if i is not None:
             arr = ev_arrays_p[i] if prof else ev_arrays[i]
-            rc = lib.msv_moe_forward_profiled(ctypes.byref(shape), ctypes.byref(ws_struct), x.data_ptr(),
-                                              logits.data_ptr(), tw.data_ptr(), tid.data_ptr(), out.data_ptr(), 0,
-                                              wsbuf.data_ptr(), nbytes, sp, arr)
+            if comm is not None:
+                rc = lib.msv_moe_forward_tp_profiled(ctypes.byref(shape), ctypes.byref(ws_struct), x.data_ptr(),
+                                                     logits.data_ptr(), tw.data_ptr(), tid.data_ptr(), out.data_ptr(),
+                                                     0, wsbuf.data_ptr(), nbytes, cref, sp, arr)
+            else:
+                rc = lib.msv_moe_forward_profiled(ctypes.byref(shape), ctypes.byref(ws_struct), x.data_ptr(),
+                                                  logits.data_ptr(), tw.data_ptr(), tid.data_ptr(), out.data_ptr(), 0,
+                                                  wsbuf.data_ptr(), nbytes, sp, arr)
+        elif comm is not None:
+            rc = lib.msv_moe_forward_tp(ctypes.byref(shape), ctypes.byref(ws_struct), x.data_ptr(), logits.data_ptr(),
+                                        tw.data_ptr(), tid.data_ptr(), out.data_ptr(), 0, wsbuf.data_ptr(), nbytes,
+                                        cref, sp)
         else:
             rc = lib.msv_moe_forward(ctypes.byref(shape), ctypes.byref(ws_struct), x.data_ptr(), logits.data_ptr(),
                                      tw.data_ptr(), tid.data_ptr(), out.data_ptr(), 0, wsbuf.data_ptr(), nbytes, sp)
         _lib.check(rc, "msv_moe_forward")
-        if tp > 1:
+        if tp > 1 and comm is None:
             if i is not None and not prof:
                 ar_ev[i][0].record(stream)
             dist.all_reduce(out)
@@ -291,7 +309,7 @@ def run_ours(args, world, rank, local):
     for j, s in enumerate(STAGES):
         if j in GEMM_EV and j + 1 in GEMM_EV:
             stage_ms[s] = statistics.mean(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(args.steps))
-    ar_ms = statistics.mean(a.elapsed_time(b) for a, b in ar_ev) if tp > 1 else 0.0
+    ar_ms = statistics.mean(a.elapsed_time(b) for a, b in ar_ev) if (tp > 1 and comm is None) else 0.0
     ms_step = ms_total / args.steps
     value = tokens * args.steps / (ms_total / 1e3)
     hbm, bf16_tf, peak_kind = peaks()
@@ -337,8 +355,8 @@ def run_ours(args, world, rank, local):
         def e2e_step():
             dx.copy_(hx, non_blocking=True)
             dl.copy_(hl, non_blocking=True)
-            o = M.moe_layer(dx, w, top_k=K_TOP, num_experts=n_exp, router_logits=dl)
-            if tp > 1:
+            o = M.moe_layer(dx, w, top_k=K_TOP, num_experts=n_exp, router_logits=dl, comm=comm)
+            if tp > 1 and comm is None:
                 dist.all_reduce(o)
             ho.copy_(o, non_blocking=True)
         for _ in range(args.warmup):
@@ -374,7 +392,11 @@ def run_ours(args, world, rank, local):
         "roofline": dict(roof, traffic=traffic_for(workload, dom)),
         "layer": {"hbm_gbs": layer_gbs, "hbm_frac": layer_gbs / hbm, "n_touched_experts": n_touched,
                   "fp8_tflops": flops / (ms_step / 1e3) / 1e12, "stage_ms": stage_ms,
-                  "allreduce_ms": ar_ms, "allreduce_share": ar_ms / ms_step if tp > 1 else 0.0},
+                  "allreduce": ("fused into the combine (peer memory)" if comm is not None
+                                else ("nccl" if tp > 1 else "none")),
+                  "allreduce_ms": ar_ms if comm is None else None,
+                  "allreduce_share": (ar_ms / ms_step if tp > 1 else 0.0) if comm is None else None,
+                  "combine_allreduce_ms": stage_ms["combine"] if comm is not None else None},
         "gpu_launches": n_launches,
         "clocks": dict(clk.summary(), window=f"timed region + {n_soak} identical untimed steps just before it"),
         "e2e": e2e,
@@ -418,6 +440,9 @@ def run_stack(args, world, rank, local):
     torch.cuda.synchronize()
     barrier()
     x = synthetic.make_hidden(tokens, H, seed=2, device=dev)
+    if tp > 1 and not args.nccl_allreduce:
+        from muserve_b200 import distributed as D
+        D.init_fused_allreduce(tokens, H)  # moe_forward then sums over the group in its combine
     stack = GraphedMoEStack(layers, batch_size=tokens, top_k=K_TOP, device=dev, norm=True, logit_biases=biases)
     # routing statistics and this library's launches per step, from one eager step
     routing = []
@@ -503,7 +528,9 @@ def run_stack(args, world, rank, local):
                    "tokens": tokens, "hidden": H, "experts": E, "top_k": K_TOP, "inter_per_rank": inter,
                    "tp": tp, "parallelism": f"tp{tp}" if tp > 1 else "single",
                    "graph": "one CUDA graph per step (norm, router GEMM, top-k, dispatch, quantise, 2 GEMMs, "
-                            "combine, NCCL all-reduce per layer)",
+                            "combine + all-reduce per layer)",
+                   "allreduce": "nccl" if (tp > 1 and args.nccl_allreduce) else
+                                ("fused into the combine (peer memory)" if tp > 1 else "none"),
                    "l2": f"no flush: each step streams {step_bytes / 1e9:.1f} GB per rank (> 126 MB L2)"},
         "step": {"ms": ms_step, "ms_per_layer": ms_step / n_layers, "hbm_gbs": gbs, "hbm_frac": gbs / hbm,
                  "peak_kind": peak_kind, "mean_touched_experts": statistics.mean(touched),
@@ -635,6 +662,8 @@ def main():
     ap.add_argument("--tokens", type=int, default=0)
     ap.add_argument("--experts", type=int, default=0, help="smaller expert count, for profiler captures only")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--nccl-allreduce", action="store_true",
+                    help="TP: plain combine + NCCL all-reduce instead of the fused peer-memory combine")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--clock-window-ms", type=float, default=500.0,
                     help="length of the clock-sampling window (0: timed region only, for profiler runs)")
@@ -653,6 +682,8 @@ def main():
             run_ours(args, world, rank, local)
     finally:
         if dist.is_initialized():
+            from muserve_b200 import distributed as D
+            D.close_fused_allreduce()  # unmaps the peers' buffers (collective)
             dist.destroy_process_group()
 
 
