@@ -281,7 +281,7 @@ int msv_ipc_close(void* ptr);
 
 /*
  * The TP group of msv_moe_forward_tp.  Every rank allocates one shared buffer of
- * msv_tp_shared_bytes(max_tokens, hidden) bytes (256-byte aligned, zero-filled: it holds the
+ * msv_tp_shared_bytes(max_tokens, hidden) bytes (256-byte aligned, zero-filled: its words carry
  * flags) and one epoch buffer of msv_tp_epoch_bytes() bytes (zero-filled), exports the shared
  * buffer and imports every other rank's.  shared[p] is rank p's buffer as mapped in this
  * process (shared[rank] is the local one).  After a MSV_ERR_TIMEOUT the buffers must be
@@ -306,10 +306,10 @@ size_t msv_tp_epoch_bytes(void);
  *   replaces: muserve/model/qwen35_layer_v2.py:657-662 with muserve/distributed.py:62-64
  *             (the per-rank result, then all_reduce(SUM) over the TP group)
  * The partials are summed in fp32 in rank order and rounded to bf16 once.  One persistent CTA
- * per SM (at most T) combines its tokens, exchanges flags with the same CTA on every rank
- * (bounded waits: MSV_ERR_TIMEOUT through msv_check_device_error), sums its H/world-column
- * slice over the ranks' partials (peer loads), writes it to every rank (peer stores), and
- * after a second flag exchange copies its rows to `out`.  T <= comm->max_tokens,
+ * per SM (at most T) combines its tokens and pushes each H/world-column slice to the rank that
+ * owns it (peer stores of 8-byte words: two bf16 values and a flag); the owner sums the slices
+ * and pushes the result to every rank, which copies its rows to `out`.  Waits are bounded
+ * (MSV_ERR_TIMEOUT through msv_check_device_error).  T <= comm->max_tokens,
  * H == comm->hidden, H % (8 * world) == 0.  Every rank must make the same calls in the same
  * order on the same number of SMs.
  */

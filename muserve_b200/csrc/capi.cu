@@ -108,9 +108,10 @@ AddressRangeFn address_range_fn() {
 std::mutex g_ipc_mu;
 std::unordered_map<uintptr_t, void*> g_ipc_bases;
 
-// one rank's shared buffer: partial rows, gathered rows, flags
-size_t tp_rows_bytes(int max_tokens, int hidden) {
-  return (((size_t)max_tokens * (size_t)hidden * 2) + 255) & ~(size_t)255;
+// one rank's shared buffer: the receive area and the result area, each max_tokens x H values
+// as 8-byte words of two bf16 values and a flag
+size_t tp_area_bytes(int max_tokens, int hidden) {
+  return (((size_t)max_tokens * (size_t)hidden * 4) + 255) & ~(size_t)255;
 }
 
 struct MapKey {
@@ -1155,16 +1156,16 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
     // flags with itself)
     CombineArArgs ar{};
     ar.c = cb;
-    const size_t rb = tp_rows_bytes(comm->max_tokens, comm->hidden);
+    const size_t rb = tp_area_bytes(comm->max_tokens, comm->hidden);
     for (int p = 0; p < comm->world; ++p) {
       uint8_t* base = static_cast<uint8_t*>(comm->shared[p]);
-      ar.part[p] = reinterpret_cast<__nv_bfloat16*>(base);
-      ar.gath[p] = reinterpret_cast<__nv_bfloat16*>(base + rb);
-      ar.flags[p] = reinterpret_cast<unsigned int*>(base + 2 * rb);
+      ar.recv[p] = reinterpret_cast<uint64_t*>(base);
+      ar.res[p] = reinterpret_cast<uint64_t*>(base + rb);
     }
     ar.epoch = comm->epoch;
     ar.world = comm->world;
     ar.rank = comm->rank;
+    ar.max_tokens = comm->max_tokens;
     ar.err = d->err_word;
     int g = L.T < d->num_sms ? L.T : d->num_sms;
     g = g < kArMaxCtas ? g : kArMaxCtas;
@@ -1258,7 +1259,7 @@ int msv_ipc_close(void* ptr) {
 
 size_t msv_tp_shared_bytes(int max_tokens, int hidden) {
   if (max_tokens <= 0 || hidden <= 0) return 0;
-  return 2 * tp_rows_bytes(max_tokens, hidden) + (size_t)2 * kMaxTpRanks * kArMaxCtas * sizeof(unsigned int);
+  return 2 * tp_area_bytes(max_tokens, hidden);
 }
 
 size_t msv_tp_epoch_bytes(void) { return (size_t)kArMaxCtas * sizeof(unsigned int); }

@@ -213,12 +213,13 @@ inline int combine_threads(int H) {
   return t < kCombineThreads ? t : kCombineThreads;
 }
 
-// One token's combined row into dst, by the whole CTA (s_row / s_w: the CTA's shared slots).
-// Each thread produces 8 consecutive channels per pass (one pass when H <= 4096).  Warp 0
-// reads the token's k slots in parallel (and orders them by expert id for the per-expert
-// modes); the channel loop loads 8 slot rows before it sums them.
-template <int MODE>
-MSV_DEVICE void combine_token(const CombineArgs& a, int t, int* s_row, float* s_w, __nv_bfloat16* dst) {
+// One token's combined row, by the whole CTA (s_row / s_w: the CTA's shared slots); each
+// 8-channel piece goes to store(first channel, 4 words of packed bf16 pairs).  Each thread
+// produces 8 consecutive channels per pass (one pass when H <= 4096).  Warp 0 reads the
+// token's k slots in parallel (and orders them by expert id for the per-expert modes); the
+// channel loop loads 8 slot rows before it sums them.
+template <int MODE, class Store>
+MSV_DEVICE void combine_token(const CombineArgs& a, int t, int* s_row, float* s_w, Store&& store) {
   __syncthreads();  // the previous token's slots are no longer read
   if (threadIdx.x < 32) {
     const int j = threadIdx.x;
@@ -294,7 +295,7 @@ MSV_DEVICE void combine_token(const CombineArgs& a, int t, int* s_row, float* s_
       const __nv_bfloat162 p = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
       ow[i] = *reinterpret_cast<const uint32_t*>(&p);
     }
-    *reinterpret_cast<uint4*>(dst + c) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+    store(c, ow);
   }
 }
 
@@ -305,7 +306,10 @@ __global__ void __launch_bounds__(kCombineThreads, 2) k_combine(CombineArgs a) {
   __shared__ int s_row[16];
   __shared__ float s_w[16];
   const int t = blockIdx.x;
-  combine_token<MODE>(a, t, s_row, s_w, a.out + (int64_t)t * a.ld_out);
+  __nv_bfloat16* dst = a.out + (int64_t)t * a.ld_out;
+  combine_token<MODE>(a, t, s_row, s_w, [&](int c, const uint32_t* ow) {
+    *reinterpret_cast<uint4*>(dst + c) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+  });
   pdl_trigger();
 }
 

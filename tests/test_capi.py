@@ -62,8 +62,8 @@ def test_workspace_sizes(lib):
     s.hidden, s.shared_inter = 4096, 512  # shared intermediate must equal routed
     assert lib.msv_moe_forward_workspace_size(ctypes.byref(s)) == 0
     assert lib.msv_ragged_gemm_workspace_size(1024, 2048) > 0
-    # fused TP combine: partial + gathered rows (256-byte aligned) + 2 x 8 x 1024 flags
-    assert lib.msv_tp_shared_bytes(256, 4096) == 2 * 256 * 4096 * 2 + 2 * 8 * 1024 * 4
+    # fused TP combine: receive + result areas, 4 bytes per value (two bf16 + a 32-bit flag per word)
+    assert lib.msv_tp_shared_bytes(256, 4096) == 2 * 256 * 4096 * 4
     assert lib.msv_tp_shared_bytes(0, 4096) == 0
     assert lib.msv_tp_epoch_bytes() == 1024 * 4
     assert lib.msv_ipc_handle_bytes() == 64
