@@ -91,6 +91,39 @@ def test_fused_rejects_bad_groups(cuda):
         moe.moe_layer(x, w, top_k=6, num_experts=64, router_logits=lg, comm=comm)
 
 
+def test_fused_wait_times_out_and_reports(cuda):
+    """Failure detection without a fault: a group of two on one GPU whose second rank never
+    runs.  Rank 0's kernel pushes its pieces and then waits for rank 1's, which never come;
+    after its 2 s limit it ends, the error word reports MSV_ERR_TIMEOUT, and the context stays
+    usable (a later plain layer gives the same bits as before)."""
+    import ctypes
+
+    from muserve_b200 import _lib
+    lib = _lib.load()
+    w = _layer(cuda)
+    x = orc.make_hidden(4, 1024, 14).to(cuda)
+    lg = orc.make_hidden(4, 64, 15).float().to(cuda)
+    ref = moe.moe_layer(x, w, top_k=6, num_experts=64, router_logits=lg)
+    moe.check_device_error()
+    bufs = [torch.zeros(lib.msv_tp_shared_bytes(16, 1024), dtype=torch.uint8, device=cuda) for _ in range(2)]
+    epoch = torch.zeros(lib.msv_tp_epoch_bytes() // 4, dtype=torch.int32, device=cuda)
+
+    class Two:
+        pass
+    comm = Two()
+    comm.struct = _lib.TpComm(world=2, rank=0, max_tokens=16, hidden=1024,
+                              shared=(ctypes.c_void_p * _lib.MAX_TP)(bufs[0].data_ptr(), bufs[1].data_ptr()),
+                              epoch=epoch.data_ptr())
+    moe.moe_layer(x, w, top_k=6, num_experts=64, router_logits=lg, comm=comm)
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="status -4"):
+        moe.check_device_error()
+    moe.check_device_error()  # the check clears the error word
+    again = moe.moe_layer(x, w, top_k=6, num_experts=64, router_logits=lg)
+    torch.cuda.synchronize()
+    assert torch.equal(again, ref)
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
