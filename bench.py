@@ -342,38 +342,78 @@ def run_ours(args, world, rank, local):
     if n_exp != E:
         workload += f"_e{n_exp}"
 
-    # e2e: through the reference-facing API from pinned host buffers, result read back each step
+    # e2e: through the reference-facing API from pinned host buffers, every step copying its input
+    # in and reading its result back.  Pipelined as a serving loop runs it: two buffer sets, the
+    # input of step i+1 (host -> device stream) and the result of step i-1 (device -> host stream)
+    # move while step i computes; events keep each buffer from being reused before it is read.
+    # The serial form (copy in, compute, copy out, one after the other) is reported beside it.
     e2e = None
     if not args.no_e2e:
         from muserve_b200 import moe as M
         hx = x.cpu().pin_memory()
         hl = logits.cpu().pin_memory()
-        ho = torch.empty(tokens, H, dtype=torch.bfloat16).pin_memory()
-        dx = torch.empty_like(x)
-        dl = torch.empty_like(logits)
+        comp = stream
+        h2d_s, d2h_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        dxs = [torch.empty_like(x) for _ in range(2)]
+        dls = [torch.empty_like(logits) for _ in range(2)]
+        outs = [torch.empty(tokens, H, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        hos = [torch.empty(tokens, H, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+        in_ready, in_free, out_ready, out_free = ([torch.cuda.Event() for _ in range(2)] for _ in range(4))
+        for b in range(2):
+            in_free[b].record(comp)
+            out_free[b].record(d2h_s)
 
-        def e2e_step():
-            dx.copy_(hx, non_blocking=True)
-            dl.copy_(hl, non_blocking=True)
-            o = M.moe_layer(dx, w, top_k=K_TOP, num_experts=n_exp, router_logits=dl, comm=comm)
+        def layer(dx, dl, o):
+            M.moe_layer(dx, w, top_k=K_TOP, num_experts=n_exp, router_logits=dl, out=o, comm=comm)
             if tp > 1 and comm is None:
                 dist.all_reduce(o)
-            ho.copy_(o, non_blocking=True)
-        for _ in range(args.warmup):
-            e2e_step()
-        barrier()
-        torch.cuda.synchronize()
-        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a0.record(stream)
-        for _ in range(args.steps):
-            e2e_step()
-        a1.record(stream)
-        torch.cuda.synchronize()
-        barrier()
-        ms_e2e = max_over_ranks(a0.elapsed_time(a1))
+
+        def piped_step(i):
+            b = i & 1
+            h2d_s.wait_event(in_free[b])
+            with torch.cuda.stream(h2d_s):
+                dxs[b].copy_(hx, non_blocking=True)
+                dls[b].copy_(hl, non_blocking=True)
+            in_ready[b].record(h2d_s)
+            comp.wait_event(in_ready[b])
+            comp.wait_event(out_free[b])
+            layer(dxs[b], dls[b], outs[b])
+            in_free[b].record(comp)
+            out_ready[b].record(comp)
+            d2h_s.wait_event(out_ready[b])
+            with torch.cuda.stream(d2h_s):
+                hos[b].copy_(outs[b], non_blocking=True)
+            out_free[b].record(d2h_s)
+
+        def serial_step(i):
+            dxs[0].copy_(hx, non_blocking=True)
+            dls[0].copy_(hl, non_blocking=True)
+            layer(dxs[0], dls[0], outs[0])
+            hos[0].copy_(outs[0], non_blocking=True)
+
+        def timed(fn):
+            for i in range(args.warmup):
+                fn(i)
+            torch.cuda.synchronize()
+            barrier()
+            torch.cuda.synchronize()
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a0.record(comp)
+            h2d_s.wait_event(a0)  # no copy starts before the timed region
+            for i in range(args.steps):
+                fn(i)
+            comp.wait_stream(d2h_s)  # the last result is on the host
+            a1.record(comp)
+            torch.cuda.synchronize()
+            barrier()
+            return max_over_ranks(a0.elapsed_time(a1))
+        ms_e2e = timed(piped_step)
+        ms_serial = timed(serial_step)
         e2e = {"value": tokens * args.steps / (ms_e2e / 1e3), "unit": "tokens/s",
-               "h2d_bytes_per_step": hx.numel() * 2 + hl.numel() * 4, "d2h_bytes_per_step": ho.numel() * 2,
-               "ms_per_step": ms_e2e / args.steps}
+               "h2d_bytes_per_step": hx.numel() * 2 + hl.numel() * 4, "d2h_bytes_per_step": hos[0].numel() * 2,
+               "ms_per_step": ms_e2e / args.steps,
+               "copies": "pipelined: step i+1's input and step i-1's result move while step i computes",
+               "serial": {"value": tokens * args.steps / (ms_serial / 1e3), "ms_per_step": ms_serial / args.steps}}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
