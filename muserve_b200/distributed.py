@@ -75,10 +75,11 @@ def barrier() -> None:
 
 class TpComm:
     """Peer-memory buffers of the TP group for the fused combine + all-reduce
-    (``msv_moe_forward_tp``).  Every rank allocates one shared buffer (partial rows, gathered
-    rows, flags) and one epoch buffer, exports the shared buffer by CUDA IPC, and maps every
-    other rank's (handles exchanged over the CPU group).  Collective: all ranks construct and
-    close it together."""
+    (``msv_moe_forward_tp``).  Every rank allocates one shared buffer (receive and result
+    areas of flagged words) and one epoch buffer, exports the shared buffer by CUDA IPC, and
+    maps every other rank's (handles exchanged over the CPU group).  Collective: all ranks
+    construct and close it together.  After a call reports MSV_ERR_TIMEOUT the group is out of step: close it
+    and build a new one (zero-filled) on every rank."""
 
     def __init__(self, max_tokens: int, hidden: int, device: torch.device | None = None):
         import ctypes

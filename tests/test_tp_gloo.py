@@ -39,6 +39,20 @@ def _worker(rank, world, port, outdir):
     part = orc.moe_forward(hid, loader.shard_moe_weights(w, world, rank, "inter"), 16, 4).float()
     D.all_reduce(part)
     torch.save(part.to(torch.bfloat16), os.path.join(outdir, f"out{rank}.pt"))
+    # fused all-reduce host logic: the IPC handles are exchanged rank-indexed over the CPU
+    # group, and moe_forward picks the buffers up only for layers that fit them
+    import torch.distributed as dist
+    got = [None] * world
+    dist.all_gather_object(got, (b"handle-%d" % rank, 256 * rank), group=D._CPU_GROUP)
+    assert got == [(b"handle-%d" % p, 256 * p) for p in range(world)]
+    assert D.fused_allreduce_comm(16, 256) is None  # not initialised
+
+    class Buffers:  # stands in for a TpComm (which needs GPUs)
+        max_tokens, hidden = 32, 256
+    D._FUSED = Buffers()
+    assert D.fused_allreduce_comm(16, 256) is D._FUSED
+    assert D.fused_allreduce_comm(33, 256) is None and D.fused_allreduce_comm(16, 512) is None
+    D._FUSED = None
     D.barrier()
     D.destroy_distributed()
 
