@@ -11,7 +11,7 @@ from __future__ import annotations
 import torch
 
 from .. import _lib, config, moe
-from ..distributed import all_reduce, get_tp_rank, get_tp_size
+from ..distributed import all_reduce, fused_allreduce_comm, get_tp_rank, get_tp_size
 from ..loader import stack_per_expert
 
 
@@ -26,8 +26,12 @@ def batched_moe_forward(hidden: torch.Tensor, weights: dict, *, top_k: int | Non
     logits = torch.nn.functional.linear(hidden, gate_w).float()
     # the shared expert joins the same launch; it is added once (rank 0) before the all-reduce,
     # which differs from the reference's post-all-reduce add only by bf16 rounding at TP > 1
+    # with the group's fused buffers (distributed.init_fused_allreduce) the combine kernel sums
+    # over the TP group itself; otherwise NCCL's all-reduce follows
+    comm = fused_allreduce_comm(hidden.shape[0], hidden.shape[1]) if tp > 1 else None
     out = moe.moe_layer(hidden.contiguous(), weights, top_k=k, num_experts=num_experts, router_logits=logits,
                         placement=1 if tp > 1 else 0, tp=tp, rank=rank, add_shared=(rank == 0),
-                        combine_mode=_lib.COMBINE_BATCHED)
-    all_reduce(out)
+                        combine_mode=_lib.COMBINE_BATCHED, comm=comm)
+    if comm is None:
+        all_reduce(out)
     return out
