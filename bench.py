@@ -231,7 +231,7 @@ def run_ours(args, world, rank, local):
     comm = None
     if tp > 1 and not args.nccl_allreduce:
         from muserve_b200 import distributed as D
-        comm = D.init_fused_allreduce(tokens, H)
+        comm = D.init_fused_allreduce(tokens, H, required=False)  # None: the peers could not be mapped
     cref = ctypes.byref(comm.struct) if comm is not None else None
 
     def step(i=None, prof=False):
@@ -433,7 +433,8 @@ def run_ours(args, world, rank, local):
         "layer": {"hbm_gbs": layer_gbs, "hbm_frac": layer_gbs / hbm, "n_touched_experts": n_touched,
                   "fp8_tflops": flops / (ms_step / 1e3) / 1e12, "stage_ms": stage_ms,
                   "allreduce": ("fused into the combine (peer memory)" if comm is not None
-                                else ("nccl" if tp > 1 else "none")),
+                                else ("none" if tp == 1 else ("nccl" if args.nccl_allreduce else
+                                                              "nccl (the peers' buffers could not be mapped)"))),
                   "allreduce_ms": ar_ms if comm is None else None,
                   "allreduce_share": (ar_ms / ms_step if tp > 1 else 0.0) if comm is None else None,
                   "combine_allreduce_ms": stage_ms["combine"] if comm is not None else None},
@@ -480,9 +481,11 @@ def run_stack(args, world, rank, local):
     torch.cuda.synchronize()
     barrier()
     x = synthetic.make_hidden(tokens, H, seed=2, device=dev)
+    fused = False
     if tp > 1 and not args.nccl_allreduce:
         from muserve_b200 import distributed as D
-        D.init_fused_allreduce(tokens, H)  # moe_forward then sums over the group in its combine
+        # moe_forward then sums over the group in its combine (None: the peers could not be mapped)
+        fused = D.init_fused_allreduce(tokens, H, required=False) is not None
     stack = GraphedMoEStack(layers, batch_size=tokens, top_k=K_TOP, device=dev, norm=True, logit_biases=biases)
     # routing statistics and this library's launches per step, from one eager step
     routing = []
@@ -569,8 +572,7 @@ def run_stack(args, world, rank, local):
                    "tp": tp, "parallelism": f"tp{tp}" if tp > 1 else "single",
                    "graph": "one CUDA graph per step (norm, router GEMM, top-k, dispatch, quantise, 2 GEMMs, "
                             "combine + all-reduce per layer)",
-                   "allreduce": "nccl" if (tp > 1 and args.nccl_allreduce) else
-                                ("fused into the combine (peer memory)" if tp > 1 else "none"),
+                   "allreduce": "none" if tp == 1 else ("fused into the combine (peer memory)" if fused else "nccl"),
                    "l2": f"no flush: each step streams {step_bytes / 1e9:.1f} GB per rank (> 126 MB L2)"},
         "step": {"ms": ms_step, "ms_per_layer": ms_step / n_layers, "hbm_gbs": gbs, "hbm_frac": gbs / hbm,
                  "peak_kind": peak_kind, "mean_touched_experts": statistics.mean(touched),

@@ -78,14 +78,16 @@ class TpComm:
     (``msv_moe_forward_tp``).  Every rank allocates one shared buffer (receive and result
     areas of flagged words) and one epoch buffer, exports the shared buffer by CUDA IPC, and
     maps every other rank's (handles exchanged over the CPU group).  Collective: all ranks
-    construct and close it together.  After a call reports MSV_ERR_TIMEOUT the group is out of step: close it
-    and build a new one (zero-filled) on every rank."""
+    construct and close it together.  Whether the mapping worked is agreed over the group: if
+    it failed on any rank, every rank unmaps what it mapped and raises the same RuntimeError.
+    After a call reports MSV_ERR_TIMEOUT the group is out of step: close it and build a new
+    one (zero-filled) on every rank."""
 
-    def __init__(self, max_tokens: int, hidden: int, device: torch.device | None = None):
+    def __init__(self, max_tokens: int, hidden: int, device: torch.device | None = None, lib=None):
         import ctypes
 
         from . import _lib
-        lib = _lib.load()
+        lib = lib if lib is not None else _lib.load()
         self.lib = lib
         self.world, self.rank = get_tp_size(), get_tp_rank()
         if self.world > _lib.MAX_TP:
@@ -93,53 +95,85 @@ class TpComm:
         if hidden % (8 * self.world):
             raise ValueError("hidden must be a multiple of 8 * world")
         dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.dev = dev
         self.max_tokens, self.hidden = max_tokens, hidden
         self.buf = torch.zeros(lib.msv_tp_shared_bytes(max_tokens, hidden), dtype=torch.uint8, device=dev)
         self.epoch = torch.zeros(lib.msv_tp_epoch_bytes() // 4, dtype=torch.int32, device=dev)
         hb = lib.msv_ipc_handle_bytes()
         handle = (ctypes.c_char * hb)()
         off = ctypes.c_uint64(0)
-        _lib.check(lib.msv_ipc_export(self.buf.data_ptr(), handle, ctypes.byref(off)), "msv_ipc_export")
-        mine = (bytes(handle), int(off.value))
-        allh = [None] * self.world
+        mine = None
+        if lib.msv_ipc_export(self.buf.data_ptr(), handle, ctypes.byref(off)) == _lib.MSV_OK:
+            mine = (bytes(handle), int(off.value))
+        allh = [mine]
         if self.world > 1:
+            allh = [None] * self.world
             dist.all_gather_object(allh, mine, group=_CPU_GROUP)
-        else:
-            allh = [mine]
         self.imported = []
         ptrs = []
-        for p, (h, o) in enumerate(allh):
+        failed = [p for p, h in enumerate(allh) if h is None]
+        for p, h in enumerate(allh):
+            if failed:
+                break
             if p == self.rank:
                 ptrs.append(self.buf.data_ptr())
                 continue
             out = ctypes.c_void_p()
-            hbuf = (ctypes.c_char * hb).from_buffer_copy(h)
-            _lib.check(lib.msv_ipc_import(hbuf, ctypes.c_uint64(o), ctypes.byref(out)), "msv_ipc_import")
+            hbuf = (ctypes.c_char * hb).from_buffer_copy(h[0])
+            if lib.msv_ipc_import(hbuf, ctypes.c_uint64(h[1]), ctypes.byref(out)) != _lib.MSV_OK:
+                failed.append(p)
+                break
             self.imported.append(out.value)
             ptrs.append(out.value)
+        # every rank learns whether any rank failed
+        if not _agree(not failed):
+            self._unmap()
+            raise RuntimeError("fused all-reduce: CUDA IPC mapping of the peers' buffers failed on a rank"
+                               + (f" (this rank: peers {failed})" if failed else ""))
         shared = (ctypes.c_void_p * _lib.MAX_TP)(*(ptrs + [None] * (_lib.MAX_TP - len(ptrs))))
         self.struct = _lib.TpComm(world=self.world, rank=self.rank, max_tokens=max_tokens, hidden=hidden,
                                   shared=shared, epoch=self.epoch.data_ptr())
-        torch.cuda.synchronize(dev)
+        if dev.type == "cuda":
+            torch.cuda.synchronize(dev)
         barrier()  # every rank's flags are zero before any rank's first call
 
-    def close(self) -> None:
-        torch.cuda.synchronize()
-        barrier()  # no rank still reads or writes another's buffer
+    def _unmap(self) -> None:
         for p in self.imported:
             self.lib.msv_ipc_close(p)
         self.imported = []
+
+    def close(self) -> None:
+        if self.dev.type == "cuda":
+            torch.cuda.synchronize(self.dev)
+        barrier()  # no rank still reads or writes another's buffer
+        self._unmap()
+
+
+def _agree(ok: bool) -> bool:
+    """True on every rank when ``ok`` is true on every rank (over the CPU group)."""
+    if not dist.is_initialized() or dist.get_world_size() == 1:
+        return ok
+    t = torch.tensor([1 if ok else 0], dtype=torch.int32)
+    dist.all_reduce(t, op=dist.ReduceOp.MIN, group=_CPU_GROUP)
+    return bool(t.item())
 
 
 _FUSED: TpComm | None = None
 
 
-def init_fused_allreduce(max_tokens: int, hidden: int) -> TpComm:
+def init_fused_allreduce(max_tokens: int, hidden: int, required: bool = True) -> TpComm | None:
     """Enable the fused combine + all-reduce for layers of up to ``max_tokens`` tokens of width
-    ``hidden`` (collective).  ``model.qwen35_layer_v2.moe_forward`` then skips ``all_reduce``."""
+    ``hidden`` (collective).  ``model.qwen35_layer_v2.moe_forward`` then skips ``all_reduce``.
+    With ``required=False`` a group whose peer buffers cannot be mapped keeps NCCL's
+    all-reduce (every rank alike) and None is returned."""
     global _FUSED
     close_fused_allreduce()
-    _FUSED = TpComm(max_tokens, hidden)
+    try:
+        _FUSED = TpComm(max_tokens, hidden)
+    except RuntimeError:
+        if required:
+            raise
+        _FUSED = None
     return _FUSED
 
 

@@ -53,8 +53,58 @@ def _worker(rank, world, port, outdir):
     assert D.fused_allreduce_comm(16, 256) is D._FUSED
     assert D.fused_allreduce_comm(33, 256) is None and D.fused_allreduce_comm(16, 512) is None
     D._FUSED = None
+    _tpcomm_agreement(D, rank, world)
     D.barrier()
     D.destroy_distributed()
+
+
+class _FakeIpcLib:
+    """Stands in for the library's IPC calls on the CPU; rank `fail_rank` cannot map a peer."""
+
+    def __init__(self, rank, fail_rank):
+        self.rank, self.fail_rank, self.closed = rank, fail_rank, []
+
+    def msv_tp_shared_bytes(self, max_tokens, hidden):
+        return max_tokens * hidden * 8
+
+    def msv_tp_epoch_bytes(self):
+        return 4096
+
+    def msv_ipc_handle_bytes(self):
+        return 64
+
+    def msv_ipc_export(self, ptr, handle, off):
+        handle[:7] = b"rank-%02d" % self.rank
+        off._obj.value = 16
+        return 0
+
+    def msv_ipc_import(self, handle, off, out):
+        if self.rank == self.fail_rank:
+            return -3
+        out._obj.value = 0x1000 * (1 + int(bytes(handle[5:7]))) + off.value
+        return 0
+
+    def msv_ipc_close(self, ptr):
+        self.closed.append(ptr)
+        return 0
+
+
+def _tpcomm_agreement(D, rank, world):
+    """TpComm settles the mapping collectively: when one rank cannot map its peers, every rank
+    unmaps and raises; otherwise every rank holds every peer's pointer."""
+    fake = _FakeIpcLib(rank, fail_rank=1)
+    with pytest.raises(RuntimeError, match="IPC mapping"):
+        D.TpComm(8, 256, device=torch.device("cpu"), lib=fake)
+    # rank 0 had mapped rank 1's buffer before the group gave up: it was unmapped again
+    assert fake.closed == ([0x1000 * 2 + 16] if rank == 0 else [])
+    fake = _FakeIpcLib(rank, fail_rank=-1)
+    c = D.TpComm(8, 256, device=torch.device("cpu"), lib=fake)
+    assert c.struct.world == world and c.struct.rank == rank
+    for p in range(world):
+        want = c.buf.data_ptr() if p == rank else 0x1000 * (1 + p) + 16
+        assert c.struct.shared[p] == want
+    c.close()
+    assert sorted(fake.closed) == sorted(0x1000 * (1 + p) + 16 for p in range(world) if p != rank)
 
 
 @pytest.mark.timeout(300)
