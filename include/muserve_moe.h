@@ -1,11 +1,13 @@
 /*
  * muserve_moe.h — C ABI of the B200 (sm_100a) FP8 mixture-of-experts path.
  *
- * Every entry point takes raw device pointers, explicit sizes and a CUDA stream, never
- * allocates device memory, never synchronises the stream, and returns an int status
+ * Every compute entry point takes raw device pointers, explicit sizes and a CUDA stream,
+ * never allocates device memory, never synchronises the stream, and returns an int status
  * (MSV_OK == 0, negative on error; msv_last_error() gives the message).  Work is enqueued
  * on `stream` only, so a caller can capture the calls in a CUDA graph (a statement this
- * header does not extend to msv_ragged_moe_gemm_fp8_noalloc).
+ * header does not extend to msv_ragged_moe_gemm_fp8_noalloc).  The exceptions are set-up and
+ * checking calls: msv_ipc_* map and unmap another process's allocation (no stream), and
+ * msv_check_device_error synchronises the stream it is given.
  *
  * Paths cited as `file:line` are in the reference project (xuguanghan/muserve); each entry
  * point names the reference interface it replaces.
