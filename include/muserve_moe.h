@@ -307,8 +307,8 @@ size_t msv_tp_epoch_bytes(void);
  * `out` receives the all-reduced [T,H] bf16 result, identical on every rank.
  *   replaces: muserve/model/qwen35_layer_v2.py:657-662 with muserve/distributed.py:62-64
  *             (the per-rank result, then all_reduce(SUM) over the TP group)
- * The partials are summed in fp32 in rank order and rounded to bf16 once.  One persistent CTA
- * per SM (at most T) combines its tokens and pushes each H/world-column slice to the rank that
+ * The partials are summed in fp32 in rank order and rounded to bf16 once.  A persistent grid
+ * no larger than the SMs hold at once (at most T CTAs) combines the tokens and pushes each H/world-column slice to the rank that
  * owns it (peer stores of 8-byte words: two bf16 values and a flag); the owner sums the slices
  * and pushes the result to every rank, which copies its rows to `out`.  Waits are bounded
  * (MSV_ERR_TIMEOUT through msv_check_device_error).  T <= comm->max_tokens,

@@ -1167,12 +1167,21 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
     ar.rank = comm->rank;
     ar.max_tokens = comm->max_tokens;
     ar.err = d->err_word;
-    int g = L.T < d->num_sms ? L.T : d->num_sms;
+    // the grid is at most what the SMs hold at once (the occupancy query for this kernel and
+    // block size), so every CTA is resident and none waits for one that cannot be scheduled
+    const int threads = combine_threads(L.H);
+    void (*kern)(CombineArArgs) = cb.mode == MSV_COMBINE_V2          ? k_combine_ar<MSV_COMBINE_V2>
+                                  : cb.mode == MSV_COMBINE_DISPATCH ? k_combine_ar<MSV_COMBINE_DISPATCH>
+                                                                    : k_combine_ar<MSV_COMBINE_BATCHED>;
+    int per_sm = 0;
+    if (int rc = cuda_check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, 0),
+                            "cudaOccupancyMaxActiveBlocksPerMultiprocessor"))
+      return rc;
+    per_sm = per_sm < 1 ? 1 : per_sm;
+    int g = per_sm * d->num_sms;
+    g = L.T < g ? L.T : g;
     g = g < kArMaxCtas ? g : kArMaxCtas;
-    const dim3 grid(g), block(combine_threads(L.H));
-    if (cb.mode == MSV_COMBINE_V2) launch_k(k_combine_ar<MSV_COMBINE_V2>, grid, block, 0, stream, ar);
-    else if (cb.mode == MSV_COMBINE_DISPATCH) launch_k(k_combine_ar<MSV_COMBINE_DISPATCH>, grid, block, 0, stream, ar);
-    else launch_k(k_combine_ar<MSV_COMBINE_BATCHED>, grid, block, 0, stream, ar);
+    launch_k(kern, dim3(g), dim3(threads), 0, stream, ar);
     if (int rc = cuda_check(cudaGetLastError(), "launch combine_ar")) return rc;
     return mark(6);
   }

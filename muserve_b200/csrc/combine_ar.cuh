@@ -5,8 +5,8 @@
 // Data moves as self-validating 8-byte words: two bf16 values and a 32-bit flag, written and
 // read as whole 64-bit elements, so a reader that sees the flag of this call sees its data, and
 // no fence or separate flag exchange is needed.  Rank p owns the column slice
-// [p*H/W, (p+1)*H/W).  Every rank runs the same persistent grid of G CTAs (G <= SMs: all
-// resident), and CTA b handles tokens b, b + G, ... on every rank:
+// [p*H/W, (p+1)*H/W).  Every rank runs the same persistent grid of G CTAs (at most what the
+// SMs hold at once: all resident), and CTA b handles tokens b, b + G, ... on every rank:
 //   A. it combines its tokens and pushes each 8-column piece to the piece's owner, into the
 //      owner's receive area at (source rank, token, column) (peer stores);
 //   B. for its tokens and this rank's slice, it waits for the W sources' words, sums them in
@@ -67,7 +67,7 @@ MSV_DEVICE bool ld_ll2(const uint64_t* p, uint32_t f, uint32_t& d0, uint32_t& d1
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(kCombineThreads, 1) k_combine_ar(CombineArArgs a) {
+__global__ void __launch_bounds__(kCombineThreads, 2) k_combine_ar(CombineArArgs a) {
   pdl_wait();
   __shared__ int s_row[16];
   __shared__ float s_w[16];
