@@ -89,3 +89,38 @@ def test_per_token_oracle_equals_staged_oracle():
     st, w, x = run_oracle(g)
     out = orc.moe_forward_tokens(x, w, st["topk_w"], st["topk_ids"])
     assert torch.equal(out, st["output"])
+
+
+def test_rms_norm_gemma_oracle_is_one_rounding():
+    """The oracle's rms_norm_gemma (qwen35_layer_v2.py:59-62, torch's rms_norm on bf16 input)
+    equals an independent numpy restatement: w = bf16(1 + weight), x * (1/sqrt(mean(x^2) + eps))
+    * w in fp32, rounded to bf16 once.  The GPU kernel is tested against this oracle."""
+    import numpy as np
+    from oracle import moe_oracle as orc
+    g = torch.Generator().manual_seed(21)
+    x = (torch.randn(16, 2048, generator=g) * 3).to(torch.bfloat16)
+    w = (torch.randn(2048, generator=g) * 0.1).to(torch.bfloat16)
+    out = orc.rms_norm_gemma(x, w)
+    xf = x.float().numpy()
+    weff = (1.0 + w.float()).to(torch.bfloat16).float().numpy()
+    ms = (xf.astype(np.float64) ** 2).mean(axis=1, keepdims=True)
+    rstd = (np.float32(1.0) / np.sqrt(ms.astype(np.float32) + np.float32(1e-6))).astype(np.float32)
+    ref = torch.from_numpy((xf * rstd * weff).astype(np.float32)).to(torch.bfloat16)
+    d = (out.view(torch.int16).int() - ref.view(torch.int16).int()).abs()
+    # the mean of squares is summed in another order here (float64): rstd may move by an ulp
+    assert d.max().item() <= 1 and (d == 0).float().mean().item() >= 0.99
+
+
+def test_route_biased_oracle():
+    """The stack benchmark's prior is a plain fp32 add before the reference's routing."""
+    from oracle import moe_oracle as orc
+    g = torch.Generator().manual_seed(22)
+    lg = torch.randn(8, 64, generator=g)
+    b = orc.zipf_bias(64, 1.2, seed=3)
+    w1, i1 = orc.route_biased(lg, b, 6)
+    w2, i2 = orc.route(lg + b, 6)
+    assert torch.equal(i1, i2) and torch.equal(w1, w2)
+    # a Zipf prior concentrates routing on the popular experts
+    _, ib = orc.route(torch.randn(4096, 64, generator=g) + b, 6)
+    top = torch.argsort(b, descending=True)[:6]
+    assert torch.isin(ib, top).float().mean() > 0.3
