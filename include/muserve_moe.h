@@ -287,7 +287,10 @@ int msv_ipc_close(void* ptr);
  * flags) and one epoch buffer of msv_tp_epoch_bytes() bytes (zero-filled), exports the shared
  * buffer and imports every other rank's.  shared[p] is rank p's buffer as mapped in this
  * process (shared[rank] is the local one).  After a MSV_ERR_TIMEOUT the buffers must be
- * zero-filled again on every rank before the next call.
+ * zero-filled again on every rank before the next call.  Calls on one group may change the
+ * token count (up to max_tokens) and the combine mode freely: the kernel's grid cap depends
+ * only on the device and `hidden`, so each token keeps its CTA (and that CTA's flag counter)
+ * from call to call.
  */
 typedef struct msv_tp_comm {
   int world;                     /* ranks in the group, 1..MSV_MAX_TP */

@@ -309,6 +309,26 @@ int launch_gemm_rows(const RowsArgs& a, cudaStream_t st, int num_sms) {
   return cuda_check(cudaGetLastError(), "launch grouped_gemm_rows");
 }
 
+// Grid cap of the fused combine + all-reduce for blocks of `threads` threads: the smallest
+// per-SM occupancy over the three combine-mode instances times the SMs, at most kArMaxCtas.
+// Independent of the mode, so a group's token-to-CTA mapping never changes between calls.
+int combine_ar_grid_cap(int threads, int num_sms, int* cap) {
+  void (*kerns[3])(CombineArArgs) = {k_combine_ar<MSV_COMBINE_V2>, k_combine_ar<MSV_COMBINE_DISPATCH>,
+                                     k_combine_ar<MSV_COMBINE_BATCHED>};
+  int per_sm = 1 << 30;
+  for (auto* k : kerns) {
+    int n = 0;
+    if (int rc = cuda_check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, threads, 0),
+                            "cudaOccupancyMaxActiveBlocksPerMultiprocessor"))
+      return rc;
+    per_sm = n < per_sm ? n : per_sm;
+  }
+  per_sm = per_sm < 1 ? 1 : per_sm;
+  const int g = per_sm * num_sms;
+  *cap = g < kArMaxCtas ? g : kArMaxCtas;
+  return MSV_OK;
+}
+
 int launch_gemm_variant(bool small, const GemmArgs& a, cudaStream_t st, int nsm) {
   return small ? launch_gemm<G2Small>(a, st, nsm) : launch_gemm<G2Large>(a, st, nsm);
 }
@@ -1167,20 +1187,18 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
     ar.rank = comm->rank;
     ar.max_tokens = comm->max_tokens;
     ar.err = d->err_word;
-    // the grid is at most what the SMs hold at once (the occupancy query for this kernel and
-    // block size), so every CTA is resident and none waits for one that cannot be scheduled
+    // The grid is at most what the SMs hold at once, so every CTA is resident and none waits
+    // for one that cannot be scheduled.  The cap must be the same for every call on a group
+    // (token t is always handled by CTA t mod cap, whose epoch flags its slots): it is the
+    // smallest occupancy of the three combine-mode instances at this H, which depends only on
+    // the device and the group's hidden size, never on the call's mode or token count.
     const int threads = combine_threads(L.H);
     void (*kern)(CombineArArgs) = cb.mode == MSV_COMBINE_V2          ? k_combine_ar<MSV_COMBINE_V2>
                                   : cb.mode == MSV_COMBINE_DISPATCH ? k_combine_ar<MSV_COMBINE_DISPATCH>
                                                                     : k_combine_ar<MSV_COMBINE_BATCHED>;
-    int per_sm = 0;
-    if (int rc = cuda_check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, 0),
-                            "cudaOccupancyMaxActiveBlocksPerMultiprocessor"))
-      return rc;
-    per_sm = per_sm < 1 ? 1 : per_sm;
-    int g = per_sm * d->num_sms;
-    g = L.T < g ? L.T : g;
-    g = g < kArMaxCtas ? g : kArMaxCtas;
+    int cap = 0;
+    if (int rc = combine_ar_grid_cap(threads, d->num_sms, &cap)) return rc;
+    const int g = L.T < cap ? L.T : cap;
     launch_k(kern, dim3(g), dim3(threads), 0, stream, ar);
     if (int rc = cuda_check(cudaGetLastError(), "launch combine_ar")) return rc;
     return mark(6);

@@ -14,7 +14,11 @@
 //      pushes the result to every rank's result area (peer stores);
 //   C. it waits for its tokens' full rows in this rank's result area and writes the output.
 // The flag is a per-CTA call counter (epoch) kept in this rank's device memory and advanced by
-// the CTA itself, identical on all ranks, so a captured CUDA graph replays correctly.  Reuse is
+// the CTA itself, identical on all ranks, so a captured CUDA graph replays correctly.  This
+// needs a fixed token-to-CTA mapping on a group: G = min(T, cap) with a cap that is the same
+// for every call (the host takes the smallest occupancy over the three combine modes at the
+// group's H), so token t is always handled by CTA t mod cap and every slot of token t only
+// ever carries that CTA's counter values, whatever T or the combine mode of a call.  Reuse is
 // ordered by the data: a rank writes a receive slot of call n+1 only after it has received the
 // owner's call-n result, which the owner computed from that slot, and it writes a result slot of
 // call n+1 only after every rank's call-n+1 pieces reached it, which each rank sends after

@@ -157,9 +157,12 @@ def _tp_worker(rank, world, ref, port, q):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("MUSERVE_REF"),
+                    help="checkout of the reference (the directory holding muserve/); or set MUSERVE_REF")
     ap.add_argument("--only", default=None)
     a = ap.parse_args()
+    if not a.ref:
+        ap.error("the reference checkout is required: --ref PATH or MUSERVE_REF=PATH")
     torch.set_num_threads(os.cpu_count())
     cases = {}
     # H=2048, 64 experts top-8, I=512, shared I=512, 32 tokens, seed 0

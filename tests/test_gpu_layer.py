@@ -1,5 +1,6 @@
 """Whole MoE layer on the GPU vs the reference (golden fixtures) and the CPU oracle, from the
-BASELINE CPU-check config to full-shape decode (64 tokens) and prefill (8192 tokens)."""
+BASELINE CPU-check config to full-shape decode (64 tokens, every token checked), prefill (8192
+tokens, every expert's tile edges checked) and skewed routing (128 tokens, every token)."""
 import pytest
 import torch
 
@@ -38,8 +39,8 @@ def test_layer_c0_on_reference_logits(c0):
 
 
 def test_moe_forward_c0_end_to_end(c0):
-    """Through the reference-shaped moe_forward (router GEMM on cuBLAS): routing compared to
-    the reference separately, output compared on tokens routed identically."""
+    """Through the reference-shaped moe_forward (the library's tcgen05 router GEMM): routing
+    compared to the reference separately, output compared on tokens routed identically."""
     g, c, w, x, wd, xd = c0
     out, tw, tid = v2.moe_forward(xd, wd, top_k=c["k"], return_routing=True)
     same = (tid.cpu().long() == g["topk_ids"]).all(-1)
@@ -85,9 +86,10 @@ def test_kernel_layer_apis(c0):
     ref = orc.moe_forward_tokens(x, routed_only, tw32, g["topk_ids"], combine="dispatch")
     assert_close_bf16(out, ref)
     out_b = batched_moe_forward(xd, dict(wd), top_k=c["k"])
-    lg = torch.nn.functional.linear(xd, wd["moe.gate.weight"]).float()
-    tw_b, tid_b = orc.route(lg.cpu(), c["k"])
-    ref_b = orc.moe_forward_tokens(x, w, tw_b, tid_b, combine="batched")
+    # batched_moe_forward routes with the library's router GEMM (deterministic); the oracle
+    # gets that same routing, and the routing itself is checked in test_gpu_router_gemm.py
+    tw_b, tid_b = moe.router_from_hidden(xd, wd["moe.gate.weight"], c["k"])
+    ref_b = orc.moe_forward_tokens(x, w, tw_b.cpu(), tid_b.cpu().long(), combine="batched")
     assert_close_bf16(out_b, ref_b)
 
 
@@ -130,19 +132,46 @@ def test_full_decode_c1(cuda, full_layer):
     rw, rid = orc.route(logits.cpu(), 10)
     assert torch.equal(tid.cpu().long(), rid)
     assert (tw.cpu().view(torch.int16).int() - rw.view(torch.int16).int()).abs().max() <= 1
-    check_sample(x, w, out, tw, tid, torch.tensor([0, 1, 17, 40, 63]))
+    check_sample(x, w, out, tw, tid, torch.arange(64))  # every token
     assert torch.isfinite(out.float()).all()
     moe.check_device_error()
 
 
+def boundary_tokens(tid: torch.Tensor, tokens: int, edges=(0, 31, 32, 127, 128, 255, 256), extra: int = 512,
+                    seed: int = 0) -> torch.Tensor:
+    """Tokens whose rows sit at the tile edges of every expert group: within each expert's rows
+    (token order, as the stable dispatch sorts them) the rows at ``edges`` and the last row, for
+    the shared expert (one row per token) the tokens at every multiple of 128 and the one before
+    it; then ``extra`` seeded random tokens."""
+    tid = tid.cpu().long()
+    pick = set()
+    for e in torch.unique(tid).tolist():
+        toks = (tid == e).any(-1).nonzero().flatten().tolist()  # ascending token order
+        for r in list(edges) + [len(toks) - 1]:
+            if 0 <= r < len(toks):
+                pick.add(toks[r])
+    for j in range(0, tokens, 128):
+        pick.update(t for t in (j - 1, j) if 0 <= t < tokens)
+    pick.add(tokens - 1)
+    g = torch.Generator().manual_seed(seed)
+    pick.update(torch.randperm(tokens, generator=g)[:extra].tolist())
+    return torch.tensor(sorted(pick))
+
+
 def test_full_prefill_c2(cuda, full_layer):
-    """8192 tokens, router gate N(0, 0.02): ~160 tokens per expert, multi-chunk tiles."""
+    """8192 tokens, router gate N(0, 0.02): ~160 tokens per expert, multi-chunk tiles.  The
+    oracle checks every expert's first and last rows and the rows on both sides of each 32-,
+    128- and 256-row tile edge (and the shared expert's 128-token edges), plus 512 random
+    tokens: well over 1000 tokens touching all 512 experts."""
     w = full_layer
     x = synthetic.make_hidden(8192, 4096, seed=4, device=cuda)
     out, tw, tid = v2.moe_forward(x, w, top_k=10, return_routing=True)
     counts = torch.bincount(tid.flatten().long(), minlength=512)
     assert counts.sum() == 8192 * 10 and counts.max() > 128  # exercises the chunked tiles
-    check_sample(x, w, out, tw, tid, torch.tensor([0, 5, 1000, 4097, 8191]))
+    sample = boundary_tokens(tid, 8192)
+    assert len(sample) >= 512
+    assert torch.unique(tid.cpu()[sample]).numel() == int((counts > 0).sum())  # every touched expert
+    check_sample(x, w, out, tw, tid, sample)
     moe.check_device_error()
 
 
@@ -155,7 +184,7 @@ def test_full_zipf_skew(cuda, full_layer):
     out, tw, tid = moe.moe_layer(x, w, top_k=10, num_experts=512, router_logits=lg.contiguous(), return_routing=True)
     counts = torch.bincount(tid.flatten().long(), minlength=512)
     assert counts.max() > 32
-    check_sample(x, w, out, tw, tid, torch.tensor([0, 64, 127]))
+    check_sample(x, w, out, tw, tid, torch.arange(128))  # every token
 
 
 def test_layer_deterministic(cuda, full_layer):

@@ -57,6 +57,23 @@ def test_fused_group_of_one_equals_combine(cuda, T, mode):
     moe.check_device_error()
 
 
+def test_fused_group_of_one_varying_calls(cuda):
+    """One group, calls whose token count (above and below the grid cap) and combine mode
+    change from call to call: each token keeps its CTA and flag counter, so every call equals
+    the plain combine bit for bit.  At H=4096 a CTA has 512 threads and the grid cap is a few
+    hundred CTAs, so 300 and 700 tokens wrap around it."""
+    w = _layer(cuda, h=4096, e=16, inter=256)
+    comm = _group_of_one(cuda, 700, 4096)
+    calls = [(300, 0), (4, 1), (37, 2), (300, 0), (700, 2), (300, 1), (1, 0), (700, 0), (300, 0)]
+    for i, (T, mode) in enumerate(calls):
+        x = orc.make_hidden(T, 4096, 40 + i).to(cuda)
+        lg = orc.make_hidden(T, 16, 60 + i).float().to(cuda)
+        ref = moe.moe_layer(x, w, top_k=4, num_experts=16, router_logits=lg, combine_mode=mode)
+        got = moe.moe_layer(x, w, top_k=4, num_experts=16, router_logits=lg, combine_mode=mode, comm=comm)
+        assert torch.equal(got, ref), (T, mode)
+    moe.check_device_error()
+
+
 def test_fused_group_of_one_in_a_graph(cuda):
     w = _layer(cuda)
     x = orc.make_hidden(64, 1024, 7).to(cuda)
@@ -190,3 +207,90 @@ def test_fused_allreduce_ranks(cuda, tmp_path, world, T):
     lg = orc.make_hidden(T, 64, 13).float()
     ref = orc.moe_forward(x, full, 64, 6, logits=lg)
     assert_close_bf16(res[0]["fused"][0].float(), ref.float())
+
+
+# ── BASELINE config 3 shapes on 2, 4 and 8 GPUs ─────────────────────────────────────────────
+
+C3 = dict(H=4096, E=512, K=10, I=1024, T=256)
+
+
+def _c3_inputs(dev):
+    from muserve_b200 import synthetic
+    w = synthetic.make_layer_weights(C3["H"], C3["E"], C3["I"], C3["I"], seed=1, device=dev)
+    x = synthetic.make_hidden(C3["T"], C3["H"], seed=2, device=dev)
+    lg = synthetic.uniform_logits(C3["T"], C3["E"], seed=3, device=dev)
+    return w, x, lg
+
+
+def _rank_main_c3(rank, world, port, result_dir):
+    os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
+                      MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+
+    from muserve_b200 import distributed as D
+    from muserve_b200.loader import shard_moe_weights
+    D.init_distributed(backend="nccl", timeout_s=60)
+    dev = torch.device("cuda", rank)
+    w, x, lg = _c3_inputs(dev)
+    shard = {k: v for k, v in shard_moe_weights(w, world, rank, "inter").items() if torch.is_tensor(v)}
+    del w
+    torch.cuda.empty_cache()
+    kw = dict(top_k=C3["K"], num_experts=C3["E"], router_logits=lg)
+    partial = moe.moe_layer(x, shard, **kw)
+    nccl = partial.clone()
+    dist.all_reduce(nccl)
+    comm = D.init_fused_allreduce(C3["T"], C3["H"])
+    fused = [moe.moe_layer(x, shard, comm=comm, **kw).clone() for _ in range(3)]
+    torch.cuda.synchronize()
+    moe.check_device_error()
+    torch.save({"partial": partial.cpu(), "nccl": nccl.cpu(), "fused": [f.cpu() for f in fused]},
+               os.path.join(result_dir, f"r{rank}.pt"))
+    D.destroy_distributed()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_fused_allreduce_c3_ranks(cuda, tmp_path, world):
+    """BASELINE config 3 (H=4096, 512 experts top-10 + shared, I/TP = 1024/world, 256 tokens)
+    on `world` GPUs, one process per GPU, through the fused combine + all-reduce: every rank
+    holds the same bits on every call; the result equals, bit for bit, the rank partials
+    summed in rank order in fp32 with one bf16 rounding (the emulated sum that
+    test_gpu_tp_c3.py checks against the oracle); each rank's partial equals the one computed
+    with its shard on GPU 0; NCCL's all-reduce agrees within the bf16 bar (bit for bit at two
+    ranks)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+
+    from muserve_b200.loader import shard_moe_weights
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main_c3, args=(r, world, port, str(tmp_path))) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=600)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            p.join()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    res = [torch.load(tmp_path / f"r{r}.pt") for r in range(world)]
+    w, x, lg = _c3_inputs(cuda)
+    total = torch.zeros(C3["T"], C3["H"], dtype=torch.float32)
+    for r in range(world):
+        wr = {k: v for k, v in shard_moe_weights(w, world, r, "inter").items() if torch.is_tensor(v)}
+        part = moe.moe_layer(x, wr, top_k=C3["K"], num_experts=C3["E"], router_logits=lg).cpu()
+        assert torch.equal(part, res[r]["partial"]), f"rank {r} partial differs from the same shard on GPU 0"
+        total += part.float()
+        del wr
+    emulated = total.to(torch.bfloat16)
+    for r in range(world):
+        for f in res[r]["fused"]:
+            assert torch.equal(f, emulated)
+        if world == 2:
+            assert torch.equal(res[r]["nccl"], emulated)
+        assert_close_bf16(res[r]["nccl"].float(), emulated.float())
+    full = moe.moe_layer(x, w, top_k=C3["K"], num_experts=C3["E"], router_logits=lg).cpu()
+    assert_close_bf16(emulated.float(), full.float())  # unsharded layer: differs by partial rounding only
+    del w
+    torch.cuda.empty_cache()
