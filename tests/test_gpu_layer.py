@@ -44,7 +44,8 @@ def test_moe_forward_c0_end_to_end(c0):
     g, c, w, x, wd, xd = c0
     out, tw, tid = v2.moe_forward(xd, wd, top_k=c["k"], return_routing=True)
     same = (tid.cpu().long() == g["topk_ids"]).all(-1)
-    assert same.float().mean() >= 0.9, f"routing differs on {int((~same).sum())} of {len(same)} tokens"
+    # measured: identical on all 32 tokens (test_gpu_routing_from_hidden.py bounds the rate)
+    assert int((~same).sum()) <= 1, f"routing differs on {int((~same).sum())} of {len(same)} tokens"
     assert_close_bf16(out.cpu()[same], g["output"][same])
 
 

@@ -12,7 +12,11 @@ mismatch rate from the hidden states is measured and bounded at the BASELINE con
 * C2: 8192 tokens at the C1 shapes (BASELINE config 2 routes from the gate).
 
 A token counts as mismatched when its ordered top-k ids differ; the bounds are the measured
-counts plus a margin (the mismatch counts are printed with the prefix ``routing-mismatch``)."""
+counts plus a margin (the mismatch counts are printed with the prefix ``routing-mismatch``).
+Measured on B200: C0 0 of 32, C1 from hidden 0 of 64, C2 12 of 8192 ordered (2 of 8192 as
+sets).  On tokens whose ids agree, the renormalised bf16 weights come from logits that may
+differ in the last bf16 bit, so they agree within a few bf16 ulp (4 measured at C2) rather
+than the 1 ulp of identical logits."""
 import pytest
 import torch
 
@@ -44,8 +48,8 @@ def test_routing_from_hidden_c0_vs_reference_golden(cuda):
     assert ordered <= 1 and ulp <= 1
 
 
-@pytest.mark.parametrize("tokens,name,bound", [(64, "c1_from_hidden", 1), (8192, "c2", 40)])
-def test_routing_from_hidden_full_shapes(cuda, tokens, name, bound):
+@pytest.mark.parametrize("tokens,name,bound,set_bound", [(64, "c1_from_hidden", 1, 1), (8192, "c2", 30, 8)])
+def test_routing_from_hidden_full_shapes(cuda, tokens, name, bound, set_bound):
     g = torch.Generator(device=cuda).manual_seed(1)
     gate = (torch.randn(512, 4096, generator=g, device=cuda) * 0.02).to(torch.bfloat16)
     x = synthetic.make_hidden(tokens, 4096, seed=4, device=cuda)
@@ -53,4 +57,4 @@ def test_routing_from_hidden_full_shapes(cuda, tokens, name, bound):
     logits = orc.bf16_linear(x.cpu(), gate.cpu()).float()  # the reference's router on the CPU
     rw, rid = orc.route(logits, 10)
     ordered, sets, ulp = _compare(tid, rid, tw, rw, name)
-    assert ordered <= bound and ulp <= 1
+    assert ordered <= bound and sets <= set_bound and ulp <= 8
