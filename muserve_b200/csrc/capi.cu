@@ -12,6 +12,7 @@
 #include "common.cuh"
 #include "grouped_gemm.cuh"
 #include "grouped_gemm_rows.cuh"
+#include "grouped_gemm_pair.cuh"
 #include "quant_combine.cuh"
 #include "route.cuh"
 #include "norm.cuh"
@@ -276,6 +277,7 @@ using G2Pair = GemmCfg<32, 2, 0, 1>;    // plain -> bf16, two 128-row blocks per
 using G2Large = GemmCfg<192, 1, 0, 3>;  // plain -> bf16, <= 192 rows per chunk
 using R1 = RowsCfg<1, 32, 2>;          // tokens on M: gate+up halves -> SwiGLU -> e4m3 (K <= 4096)
 using R2 = RowsCfg<0, 8, 4>;           // tokens on M: plain -> bf16 (K <= 1024)
+using P1 = PairCfg<32, 2>;             // CTA pairs, 256 tokens x 128 channels: gate+up -> SwiGLU -> e4m3 (K <= 4096)
 
 template <class C>
 int launch_gemm(const GemmArgs& a, cudaStream_t st, int num_sms) {
@@ -327,6 +329,45 @@ int combine_ar_grid_cap(int threads, int num_sms, int* cap) {
   const int g = per_sm * num_sms;
   *cap = g < kArMaxCtas ? g : kArMaxCtas;
   return MSV_OK;
+}
+
+// CTA-pair kernels: 2-CTA clusters, as many as can be resident at once (persistent).
+template <class C>
+int launch_gemm_pair(const RowsArgs& a, cudaStream_t st, int num_sms) {
+  static int npairs[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (!npairs[dev]) {
+    if (int rc = cuda_check(cudaFuncSetAttribute(k_grouped_gemm_pair<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 C::SMEM_BYTES),
+                            "cudaFuncSetAttribute(grouped_gemm_pair)"))
+      return rc;
+    cfg.gridDim = dim3((unsigned)(num_sms & ~1));
+    int n = 0;
+    if (int rc = cuda_check(cudaOccupancyMaxActiveClusters(&n, k_grouped_gemm_pair<C>, &cfg),
+                            "cudaOccupancyMaxActiveClusters(grouped_gemm_pair)"))
+      return rc;
+    if (n < 1) return fail(MSV_ERR_UNSUPPORTED, "grouped_gemm_pair: no 2-CTA cluster fits on this device");
+    npairs[dev] = n < num_sms / 2 ? n : num_sms / 2;
+  }
+  cfg.gridDim = dim3((unsigned)(2 * npairs[dev]));
+  cfg.numAttrs = 2;
+  g_launch_count.fetch_add(1, std::memory_order_relaxed);
+  if (int rc = cuda_check(cudaLaunchKernelEx(&cfg, k_grouped_gemm_pair<C>, a), "launch grouped_gemm_pair")) return rc;
+  return cuda_check(cudaGetLastError(), "launch grouped_gemm_pair");
 }
 
 int launch_gemm_variant(bool small, const GemmArgs& a, cudaStream_t st, int nsm) {
@@ -776,7 +817,7 @@ int msv_gemm_fp8_nt_groupwise(const uint8_t* a, const float* a_scale, int M, int
 namespace {
 struct LayerPlan {
   int T, H, E, k, I, Is, P, rows, e_local;
-  bool shared, small1, small2, rows1, rows2, gather, pair2;
+  bool shared, small1, small2, rows1, rows2, cg2, gather, pair2;
   int bn1, bn2, nb1, nb2, srows;
   size_t cap1, cap2;
 };
@@ -810,7 +851,10 @@ int plan_layer(const msv_moe_shape* s, LayerPlan* L) {
   // at most 32; other large shapes use the weight-rows kernels.
   L->rows1 = !L->small1 && (L->H / 128) % 4 == 0 && L->H / 128 <= R1::MAXKB;
   L->rows2 = !L->small2 && (L->I / 128) % 4 == 0 && L->I / 128 <= R2::MAXKB;
-  L->bn1 = L->rows1 ? R1::BM : G1Small::BN;
+  // the gate_up GEMM of those shapes runs on CTA pairs (256-row chunks); the down GEMM keeps
+  // the single-CTA token-rows kernel, which measured faster than a pair form at K = 1024
+  L->cg2 = L->rows1 && L->H / 128 <= P1::MAXKB;
+  L->bn1 = L->cg2 ? 2 * P1::BM : L->rows1 ? R1::BM : G1Small::BN;
   L->bn2 = L->rows2 ? R2::BM : (L->small2 ? G2Small::BN : G2Large::BN);
   // small-batch down GEMM: two 128-row blocks of H per tile, so each pipeline stage carries as
   // many weight bytes as the gate_up GEMM's (gate + up)
@@ -1018,7 +1062,42 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
   // 4. gate_up GEMM with SwiGLU + requant epilogue
   const uint64_t gu_rows = (uint64_t)(L.e_local - 1) * W->gu_expert_rows + L.I;
   const int nkb1 = L.H / 128, nkb2 = L.I / 128;
-  if (L.rows1) {
+  if (L.cg2) {
+    RowsArgs r{};
+    if (int rc = tensor_map(&r.tmTok, w.xq, L.rows, L.H, L.H, 64)) return rc;  // 64-row token boxes
+    if (int rc = tensor_map(&r.tmW[0][0], W->gate_w, gu_rows, L.H, L.H, 64)) return rc;
+    if (int rc = tensor_map(&r.tmW[0][1], W->up_w, gu_rows, L.H, L.H, 64)) return rc;
+    const int64_t rpe = W->gu_scale_expert_stride / nkb1;  // scale rows between experts
+    const uint64_t gs_rows = (uint64_t)(L.e_local - 1) * rpe + L.I / 128;
+    if (int rc = tensor_map_f32(&r.tmWS[0][0], W->gate_s, gs_rows, nkb1, (uint64_t)nkb1 * 4, nkb1, 1)) return rc;
+    if (int rc = tensor_map_f32(&r.tmWS[0][1], W->up_s, gs_rows, nkb1, (uint64_t)nkb1 * 4, nkb1, 1)) return rc;
+    if (L.shared) {
+      if (int rc = tensor_map(&r.tmW[1][0], W->sh_gate_w, L.Is, L.H, L.H, 64)) return rc;
+      if (int rc = tensor_map(&r.tmW[1][1], W->sh_up_w, L.Is, L.H, L.H, 64)) return rc;
+      if (int rc = tensor_map_f32(&r.tmWS[1][0], W->sh_gate_s, L.Is / 128, nkb1, (uint64_t)nkb1 * 4, nkb1, 1)) return rc;
+      if (int rc = tensor_map_f32(&r.tmWS[1][1], W->sh_up_s, L.Is / 128, nkb1, (uint64_t)nkb1 * 4, nkb1, 1)) return rc;
+    } else {
+      r.tmW[1][0] = r.tmW[0][0];
+      r.tmW[1][1] = r.tmW[0][1];
+      r.tmWS[1][0] = r.tmWS[0][0];
+      r.tmWS[1][1] = r.tmWS[0][1];
+    }
+    if (int rc = tensor_map_f32(&r.tmAS, w.xs, nkb1, L.srows, (uint64_t)L.srows * 4, P1::SC_LD, nkb1)) return rc;
+    r.w_rows[0] = (int)W->gu_expert_rows;
+    r.w_rows[1] = 0;
+    r.ws_rows[0] = (int)rpe;
+    r.ws_rows[1] = 0;
+    r.tiles = w.tiles1;
+    r.num_tiles = w.ntiles1;
+    r.num_kb = nkb1;
+    r.out = w.aq;
+    r.out_ld = L.I;
+    r.out_scale = w.as;
+    r.os_row = 1;
+    r.os_kb = L.srows;
+    r.err = d->err_word;
+    if (int rc = launch_gemm_pair<P1>(r, stream, d->num_sms)) return rc;
+  } else if (L.rows1) {
     RowsArgs r{};
     if (int rc = tensor_map_kblocks(&r.tmTok, w.xq, L.rows, L.H, L.H, R1::BM, R1::KS)) return rc;
     if (int rc = tensor_map(&r.tmW[0][0], W->gate_w, gu_rows, L.H, L.H, 64)) return rc;
