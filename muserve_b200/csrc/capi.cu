@@ -9,6 +9,7 @@
 #include <unordered_map>
 
 #include "combine_ar.cuh"
+#include "dispatch_quant.cuh"
 #include "common.cuh"
 #include "grouped_gemm.cuh"
 #include "grouped_gemm_rows.cuh"
@@ -817,7 +818,7 @@ int msv_gemm_fp8_nt_groupwise(const uint8_t* a, const float* a_scale, int M, int
 namespace {
 struct LayerPlan {
   int T, H, E, k, I, Is, P, rows, e_local;
-  bool shared, small1, small2, rows1, rows2, cg2, gather, pair2;
+  bool shared, small1, small2, rows1, rows2, cg2, pair2;
   int bn1, bn2, nb1, nb2, srows;
   size_t cap1, cap2;
 };
@@ -862,8 +863,6 @@ int plan_layer(const msv_moe_shape* s, LayerPlan* L) {
   L->nb1 = L->I / 128;
   L->nb2 = L->pair2 ? L->H / 256 : L->H / 128;
   L->srows = (L->rows + 3) & ~3;  // K-block stride of the activation scales (16-byte rows)
-  // large batches quantise each token once and gather the e4m3 rows (16-byte scale rows)
-  L->gather = L->P > kPermSingleMax && (L->H / 128) % 4 == 0;
   L->cap1 = tile_cap(L->e_local, L->P, L->bn1, L->nb1) + (size_t)L->nb1 * ((L->T + L->bn1 - 1) / L->bn1 + 1);
   L->cap2 = tile_cap(L->e_local, L->P, L->bn2, L->nb2) + (size_t)L->nb2 * ((L->T + L->bn2 - 1) / L->bn2 + 1);
   return MSV_OK;
@@ -875,8 +874,8 @@ struct LayerWs {
   int4 *tiles1, *tiles2;
   int *blk_hist, *blk_nloc, *lrank, *lpos;  // multi-block dispatch scratch
   int *ntiles1, *ntiles2;
-  uint8_t *xq, *aq, *xq_tok;
-  float *xs, *as, *gate_val, *xs_tok;
+  uint8_t *xq, *aq;
+  float *xs, *as, *gate_val;
   __nv_bfloat16* down;
 };
 
@@ -903,8 +902,6 @@ size_t carve_layer(const LayerPlan& L, uint8_t* base, LayerWs* w) {
   w->blk_nloc = c.take<int>((size_t)(nblk > 0 ? nblk : 1));
   w->lrank = c.take<int>((size_t)(L.P > 0 ? L.P : 1));
   w->lpos = c.take<int>((size_t)(L.P > 0 ? L.P : 1));
-  w->xq_tok = L.gather ? c.take<uint8_t>((size_t)L.T * L.H) : nullptr;
-  w->xs_tok = L.gather ? c.take<float>((size_t)L.T * (L.H / 128)) : nullptr;
   return c.off + 256;
 }
 }  // namespace
@@ -940,6 +937,8 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
   if (s->combine_mode < 0 || s->combine_mode > 2) return fail(MSV_ERR_INVALID, "msv_moe_forward: combine_mode");
   if (!is_pow2_aligned(hidden, 16) || !is_pow2_aligned(out, 16))
     return fail(MSV_ERR_INVALID, "msv_moe_forward: hidden/out must be 16-byte aligned");
+  if (W->sh_gate_logit_w && !is_pow2_aligned(W->sh_gate_logit_w, 16))
+    return fail(MSV_ERR_INVALID, "msv_moe_forward: the shared-expert gate weight must be 16-byte aligned");
   if (L.T == 0) return MSV_OK;
   LayerWs w;
   const size_t need = carve_layer(L, nullptr, &w);
@@ -986,17 +985,39 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
   p.shared_rows = do_shared ? L.T : 0;
   p.row_base_shared = L.P;
   if (int rc = mark(1)) return rc;
+  // 3. quantisation: each token once, its e4m3 row and scales written to every sorted row that
+  //    reads it (the routed slots the dispatch placed, then the shared expert's row)
+  ScatterArgs q{};
+  q.x = static_cast<const __nv_bfloat16*>(hidden);
+  q.ldx = L.H;
+  q.K = L.H;
+  q.T = L.T;
+  q.k = L.k;
+  q.slot_row = w.slot_row;
+  q.shared_row0 = do_shared ? L.P : -1;
+  q.q = w.xq;
+  q.ldq = L.H;
+  q.scale = w.xs;
+  q.s_kb = L.srows;
+  q.gate_w = (do_shared && W->sh_gate_logit_w) ? static_cast<const __nv_bfloat16*>(W->sh_gate_logit_w) : nullptr;
+  q.gate_val = w.gate_val;
   if (L.P <= kPermSingleMax) {
-    // one block: the whole stable counting sort and the tile lists
-    const size_t psm = permute_smem_bytes(L.e_local);
-    if (psm > 48 * 1024)
-      if (int rc = cuda_check(cudaFuncSetAttribute(k_permute, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psm),
-                              "cudaFuncSetAttribute(permute)"))
-        return rc;
-    launch_k(k_permute, dim3(1), dim3(kPermThreads), psm, stream, p);
-    if (int rc = cuda_check(cudaGetLastError(), "launch permute")) return rc;
+    // decode-sized batches: dispatch and quantisation in one launch; every CTA recounts the
+    // routing and places its own tokens (at most kDqMaxSlots slots per CTA)
+    const size_t dsm = dispatch_quant_smem_bytes(L.P, L.e_local);
+    if (int rc = cuda_check(cudaFuncSetAttribute(k_dispatch_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dsm),
+                            "cudaFuncSetAttribute(dispatch_quant)"))
+      return rc;
+    const int per_cta = kDqMaxSlots / L.k;  // tokens a CTA may take
+    int g = L.T < d->num_sms ? L.T : d->num_sms;
+    const int need = (L.T + per_cta - 1) / per_cta;
+    g = g > need ? g : need;
+    launch_k(k_dispatch_quant, dim3(g), dim3(kDqThreads), dsm, stream, p, q);
+    if (int rc = cuda_check(cudaGetLastError(), "launch dispatch_quant")) return rc;
+    if (int rc = mark(2)) return rc;
   } else {
-    // the same sort over blocks of slots: counts, one scan block (+ tile lists), scatter
+    // the same stable counting sort over blocks of slots: counts, one scan block (+ tile
+    // lists), scatter; then the quantisation
     PermuteScratch ps{w.blk_hist, w.blk_nloc, w.lrank, w.lpos, (L.P + kPermThreads - 1) / kPermThreads};
     const size_t csm = perm_count_smem_bytes(L.e_local);
     if (csm > 48 * 1024)
@@ -1009,54 +1030,9 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
     if (int rc = cuda_check(cudaGetLastError(), "launch perm_scan")) return rc;
     launch_k(k_perm_scatter, dim3((L.P + 255) / 256), dim3(256), 0, stream, p, ps);
     if (int rc = cuda_check(cudaGetLastError(), "launch perm_scatter")) return rc;
-  }
-  if (int rc = mark(2)) return rc;
-  // 3. gather + quantise (routed rows in expert order, then the shared expert's rows)
-  QuantArgs q{};
-  q.x = static_cast<const __nv_bfloat16*>(hidden);
-  q.ldx = L.H;
-  q.K = L.H;
-  q.gate_w = (do_shared && W->sh_gate_logit_w) ? static_cast<const __nv_bfloat16*>(W->sh_gate_logit_w) : nullptr;
-  q.gate_val = w.gate_val;
-  if (L.gather) {
-    // every token once, in token order (segment B computes the shared-expert gate too) ...
-    q.rows_a = 0;
-    q.rows_b = L.T;
-    q.q = w.xq_tok;
-    q.ldq = L.H;
-    q.scale = w.xs_tok;
-    q.s_row = L.H / 128;
-    q.s_kb = 1;
-    if (!do_shared) q.gate_w = nullptr;
-    launch_k(k_quant_rows, dim3((L.T + kQuantRowsPerCta - 1) / kQuantRowsPerCta), dim3(kQuantWarps * 32), 0, stream, q);
-    if (int rc = cuda_check(cudaGetLastError(), "launch quant")) return rc;
-    // ... then the routed (and shared-expert) rows copied into expert-sorted order
-    GatherArgs g{};
-    g.qt = w.xq_tok;
-    g.st = w.xs_tok;
-    g.K = L.H;
-    g.rows_a = L.P;
-    g.row_token = w.row_token;
-    g.nvalid = w.num_local;
-    g.rows_b = do_shared ? L.T : 0;
-    g.q = w.xq;
-    g.scale = w.xs;
-    g.s_kb = L.srows;
-    const int gwarps = (L.rows + 31) / 32;
-    launch_k(k_gather_rows, dim3((gwarps + kGatherWarps - 1) / kGatherWarps), dim3(kGatherWarps * 32), 0, stream, g);
-    if (int rc = cuda_check(cudaGetLastError(), "launch gather")) return rc;
-  } else {
-    q.rows_a = L.P;
-    q.idx_a = w.row_token;
-    q.nvalid_a = w.num_local;
-    q.rows_b = do_shared ? L.T : 0;
-    q.q = w.xq;
-    q.ldq = L.H;
-    q.scale = w.xs;
-    q.s_row = 1;
-    q.s_kb = L.srows;
-    launch_k(k_quant_rows, dim3((L.rows + kQuantRowsPerCta - 1) / kQuantRowsPerCta), dim3(kQuantWarps * 32), 0, stream, q);
-    if (int rc = cuda_check(cudaGetLastError(), "launch quant")) return rc;
+    if (int rc = mark(2)) return rc;
+    launch_k(k_quant_scatter, dim3(L.T), dim3(kScatterThreads), 0, stream, q);
+    if (int rc = cuda_check(cudaGetLastError(), "launch quant_scatter")) return rc;
   }
   if (int rc = mark(3)) return rc;
   // 4. gate_up GEMM with SwiGLU + requant epilogue

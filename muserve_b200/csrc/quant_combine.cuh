@@ -119,70 +119,92 @@ __global__ void __launch_bounds__(kQuantWarps * 32) k_quant_rows(QuantArgs a) {
   pdl_trigger();
 }
 
-// Large batches quantise every token once (k_quant_rows over the T token rows, into a
-// token-ordered buffer) and then copy the e4m3 rows and their scales into the expert-sorted
-// order the GEMMs read: a token's 128-channel blocks quantise the same way in every expert it
-// is routed to, so this equals quantising each gathered row, with one eleventh of the
-// arithmetic and HBM reads of the per-row form.
-struct GatherArgs {
-  const uint8_t* qt;       // [T, K] e4m3, token order
-  const float* st;         // [T, K/128] scales, token order
-  int K;
-  int rows_a;              // routed rows [0, rows_a) read token row_token[r]; rows at or
-  const int32_t* row_token;  // beyond *nvalid are skipped
-  const int32_t* nvalid;
-  int rows_b;              // shared-expert rows [rows_a, rows_a + rows_b) read token r - rows_a
-  uint8_t* q;              // [rows, K] e4m3, sorted order
-  float* scale;            // element (r, kb) at scale[kb * s_kb + r]
+// Layer path: every token is quantised once and its e4m3 row and scales are written to each
+// sorted row that reads it (its k routed slots, as the dispatch placed them, and its
+// shared-expert row).  A token's 128-channel blocks quantise the same way in every expert it is
+// routed to, so this equals quantising each gathered row (qwen35_layer_v2.py:578, :612), with one
+// eleventh of the arithmetic and of the reads.  One CTA per token, 8 channels per thread and
+// pass; a 128-channel block is 16 lanes, so its amax is a 4-step xor shuffle.
+struct ScatterArgs {
+  const __nv_bfloat16* x;
+  int64_t ldx;
+  int K, T, k;
+  const int32_t* slot_row;  // [T*k] sorted row of each slot, -1 when the slot is not on this rank
+  int shared_row0;          // >= 0: token t's shared-expert row is shared_row0 + t
+  uint8_t* q;               // [rows, K] e4m3, sorted order
+  int64_t ldq;
+  float* scale;             // element (row, kb) at scale[kb * s_kb + row]
   int64_t s_kb;
+  // shared-expert gate: gv[t] = bf16(sigmoid(bf16(x[t] . wg)))
+  const __nv_bfloat16* gate_w;
+  float* gate_val;
 };
 
-constexpr int kGatherWarps = 8;
+constexpr int kScatterThreads = 512;
+constexpr int kScatterMaxDst = 17;  // k <= 16 routed slots + the shared-expert row
 
-// A warp moves 32 consecutive rows: each row's bytes with 16-byte lanes, then the 32 rows'
-// scales one K block at a time (lane = row, so each K block is one coalesced store).
-__global__ void __launch_bounds__(kGatherWarps * 32) k_gather_rows(GatherArgs a) {
+__global__ void __launch_bounds__(kScatterThreads) k_quant_scatter(ScatterArgs a) {
   pdl_wait();
-  const int lane = threadIdx.x & 31;
-  const int r0 = (blockIdx.x * kGatherWarps + (threadIdx.x >> 5)) * 32;
-  const int rows = a.rows_a + a.rows_b;
-  if (r0 >= rows) return;
-  const int nvalid = a.nvalid ? *a.nvalid : a.rows_a;
-  // source token of row r0 + lane (-1: skip)
-  int tok = -1;
-  const int rl = r0 + lane;
-  if (rl < a.rows_a) tok = rl < nvalid ? a.row_token[rl] : -1;
-  else if (rl < rows) tok = rl - a.rows_a;
-  const int n16 = a.K / 16;  // 16-byte chunks per row
-  for (int i = 0; i < 32; ++i) {
-    const int t = __shfl_sync(0xffffffffu, tok, i);
-    if (t < 0) continue;
-    const uint4* __restrict__ src = reinterpret_cast<const uint4*>(a.qt + (int64_t)t * a.K);
-    uint4* __restrict__ dst = reinterpret_cast<uint4*>(a.q + (int64_t)(r0 + i) * a.K);
-    for (int c0 = 0; c0 < n16; c0 += 32 * 8) {
-      uint4 v[8];
+  __shared__ int s_dst[kScatterMaxDst];
+  __shared__ float s_dot[kScatterThreads / 32];
+  const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x < kScatterMaxDst) {
+    const int j = threadIdx.x;
+    int r = -1;
+    if (j < a.k) r = a.slot_row[(int64_t)t * a.k + j];
+    else if (j == a.k && a.shared_row0 >= 0) r = a.shared_row0 + t;
+    s_dst[j] = r;
+  }
+  __syncthreads();
+  const int ndst = a.k + 1;
+  const __nv_bfloat16* __restrict__ xr = a.x + (int64_t)t * a.ldx;
+  float dot = 0.f;
+  for (int c = threadIdx.x * 8; c < a.K; c += kScatterThreads * 8) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(xr + c);
+    const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+    float f[8];
+    float am = 0.f;
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int c = c0 + u * 32 + lane;
-        if (c < n16) v[u] = src[c];
-      }
+    for (int i = 0; i < 8; ++i) {
+      f[i] = bf16_bits_to_f32(w4[i >> 1], i & 1);
+      am = nanmax(am, fabsf(f[i]));
+    }
+    if (a.gate_w) {
+      const uint4 wraw = *reinterpret_cast<const uint4*>(a.gate_w + c);
+      const uint32_t g4[4] = {wraw.x, wraw.y, wraw.z, wraw.w};
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int c = c0 + u * 32 + lane;
-        if (c < n16) dst[c] = v[u];
-      }
+      for (int i = 0; i < 8; ++i) dot = fmaf(f[i], bf16_bits_to_f32(g4[i >> 1], i & 1), dot);
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) am = nanmax(am, __shfl_xor_sync(0xffffffffu, am, o));
+    // s = clamp(amax, min=1e-12) / 448 (NaN propagates as in torch.clamp)
+    const float sc = (am != am) ? am : __fdiv_rn(fmaxf(am, 1e-12f), 448.0f);
+    uint32_t packed[2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float lo = clamp_pm(__fdiv_rn(f[2 * i], sc), 448.0f);
+      const float hi = clamp_pm(__fdiv_rn(f[2 * i + 1], sc), 448.0f);
+      const uint16_t pr = f32x2_to_e4m3x2(lo, hi);
+      if (i & 1) packed[i >> 1] |= (uint32_t)pr << 16;
+      else packed[i >> 1] = pr;
+    }
+    const uint2 qv = make_uint2(packed[0], packed[1]);
+    for (int d = 0; d < ndst; ++d) {
+      const int r = s_dst[d];
+      if (r < 0) continue;
+      *reinterpret_cast<uint2*>(a.q + (int64_t)r * a.ldq + c) = qv;
+      if ((lane & 15) == 0) a.scale[(int64_t)(c / 128) * a.s_kb + r] = sc;
     }
   }
-  // scales: K/128 is a multiple of 4 on this path (16-byte rows of token scales)
-  const int nkb = a.K / 128;
-  if (tok >= 0) {
-    const float4* sp = reinterpret_cast<const float4*>(a.st + (int64_t)tok * nkb);
-    for (int kb = 0; kb < nkb; kb += 4) {
-      const float4 v = sp[kb / 4];
-      a.scale[(int64_t)(kb + 0) * a.s_kb + rl] = v.x;
-      a.scale[(int64_t)(kb + 1) * a.s_kb + rl] = v.y;
-      a.scale[(int64_t)(kb + 2) * a.s_kb + rl] = v.z;
-      a.scale[(int64_t)(kb + 3) * a.s_kb + rl] = v.w;
+  if (a.gate_w) {
+    dot = warp_sum(dot);
+    if (lane == 0) s_dot[warp] = dot;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float d = 0.f;
+      for (int w = 0; w < kScatterThreads / 32; ++w) d += s_dot[w];
+      const float lg = bf16_round(d);
+      a.gate_val[t] = bf16_round(1.0f / (1.0f + expf(-lg)));
     }
   }
   pdl_trigger();
