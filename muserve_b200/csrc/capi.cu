@@ -1258,7 +1258,7 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
     if (int rc = cuda_check(cudaGetLastError(), "launch combine_ar")) return rc;
     return mark(6);
   }
-  launch_combine(cb, stream);
+  launch_combine(cb, stream, d->num_sms);
   if (int rc = cuda_check(cudaGetLastError(), "launch combine")) return rc;
   return mark(6);
 }

@@ -241,7 +241,9 @@ inline int combine_threads(int H) {
 // token's k slots in parallel (and orders them by expert id for the per-expert modes); the
 // channel loop loads 8 slot rows before it sums them.
 template <int MODE, class Store>
-MSV_DEVICE void combine_token(const CombineArgs& a, int t, int* s_row, float* s_w, Store&& store) {
+MSV_DEVICE void combine_token(const CombineArgs& a, int t, int* s_row, float* s_w, Store&& store, int c_begin = 0,
+                              int c_end = -1) {
+  if (c_end < 0) c_end = a.H;
   __syncthreads();  // the previous token's slots are no longer read
   if (threadIdx.x < 32) {
     const int j = threadIdx.x;
@@ -269,7 +271,7 @@ MSV_DEVICE void combine_token(const CombineArgs& a, int t, int* s_row, float* s_
   }
   __syncthreads();
   const float gv = (a.add_shared && a.gate_val) ? a.gate_val[t] : 1.0f;
-  for (int c = threadIdx.x * 8; c < a.H; c += blockDim.x * 8) {
+  for (int c = c_begin + threadIdx.x * 8; c < c_end; c += blockDim.x * 8) {
     float acc[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.f;
@@ -321,7 +323,9 @@ MSV_DEVICE void combine_token(const CombineArgs& a, int t, int* s_row, float* s_
   }
 }
 
-// One CTA per token (two CTAs per SM keep enough rows in flight at large batches).
+// One CTA per token and column slice: blockIdx.y of gridDim.y takes an equal share of the
+// 8-column pieces, so small batches still spread their row loads over every SM (two CTAs per SM
+// keep enough rows in flight at large batches).
 template <int MODE>
 __global__ void __launch_bounds__(kCombineThreads, 2) k_combine(CombineArgs a) {
   pdl_wait();
@@ -329,14 +333,29 @@ __global__ void __launch_bounds__(kCombineThreads, 2) k_combine(CombineArgs a) {
   __shared__ float s_w[16];
   const int t = blockIdx.x;
   __nv_bfloat16* dst = a.out + (int64_t)t * a.ld_out;
+  const int pieces = a.H / 8, per = (pieces + gridDim.y - 1) / gridDim.y;
+  const int c_begin = (int)blockIdx.y * per * 8;
+  const int c_end = min(a.H, c_begin + per * 8);
   combine_token<MODE>(a, t, s_row, s_w, [&](int c, const uint32_t* ow) {
     *reinterpret_cast<uint4*>(dst + c) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
-  });
+  }, c_begin, c_end);
   pdl_trigger();
 }
 
-inline void launch_combine(const CombineArgs& a, cudaStream_t stream) {
-  const dim3 grid(a.T), block(combine_threads(a.H));
+// Column slices per token: enough CTAs for two per SM when the batch alone does not give them.
+inline int combine_slices(int T, int H, int num_sms) {
+  int s = T > 0 ? (2 * num_sms + T - 1) / T : 1;
+  const int max_s = H / (8 * 32) > 0 ? H / (8 * 32) : 1;  // at least one warp of pieces per slice
+  int p = 1;  // a power of two, so the slices split H / 8 pieces evenly
+  while (p < s && p < 8 && p * 2 <= max_s) p *= 2;
+  return p;
+}
+
+inline void launch_combine(const CombineArgs& a, cudaStream_t stream, int num_sms) {
+  const int sl = combine_slices(a.T, a.H, num_sms);
+  const int pieces_per = (a.H / 8 + sl - 1) / sl;
+  const int th = ((pieces_per + 31) / 32) * 32;
+  const dim3 grid(a.T, sl), block(th < kCombineThreads ? th : kCombineThreads);
   if (a.mode == MSV_COMBINE_V2) launch_k(k_combine<MSV_COMBINE_V2>, dim3(grid), dim3(block), 0, stream, a);
   else if (a.mode == MSV_COMBINE_DISPATCH) launch_k(k_combine<MSV_COMBINE_DISPATCH>, dim3(grid), dim3(block), 0, stream, a);
   else launch_k(k_combine<MSV_COMBINE_BATCHED>, dim3(grid), dim3(block), 0, stream, a);
