@@ -742,9 +742,17 @@ __global__ void __launch_bounds__(kPermThreads) k_perm_scan(PermuteArgs p, Permu
   int4* info = reinterpret_cast<int4*>(scan_sm);
   int* counts = scan_sm + 4 * E;
   int* offsets = counts + E;
+  // per-expert totals over the blocks, 16 blocks' counts in flight at a time
+  constexpr int kB = 16;
   for (int x = threadIdx.x; x < E; x += kPermThreads) {
     int c = 0;
-    for (int b = 0; b < s.nblk; ++b) c += s.blk_hist[b * E + x];
+    for (int b0 = 0; b0 < s.nblk; b0 += kB) {
+      int v[kB];
+#pragma unroll
+      for (int i = 0; i < kB; ++i) v[i] = b0 + i < s.nblk ? s.blk_hist[(b0 + i) * E + x] : 0;
+#pragma unroll
+      for (int i = 0; i < kB; ++i) c += v[i];
+    }
     counts[x] = c;
   }
   __syncthreads();
@@ -758,20 +766,29 @@ __global__ void __launch_bounds__(kPermThreads) k_perm_scan(PermuteArgs p, Permu
   __syncthreads();
   for (int x = threadIdx.x; x < E; x += kPermThreads) {
     int run = offsets[x];
-    for (int b = 0; b < s.nblk; ++b) {
-      const int c = s.blk_hist[b * E + x];
-      s.blk_hist[b * E + x] = run;
-      run += c;
+    for (int b0 = 0; b0 < s.nblk; b0 += kB) {
+      int v[kB];
+#pragma unroll
+      for (int i = 0; i < kB; ++i) v[i] = b0 + i < s.nblk ? s.blk_hist[(b0 + i) * E + x] : 0;
+#pragma unroll
+      for (int i = 0; i < kB; ++i)
+        if (b0 + i < s.nblk) {
+          s.blk_hist[(b0 + i) * E + x] = run;
+          run += v[i];
+        }
     }
     if (p.expert_counts) p.expert_counts[x] = counts[x];
   }
-  // exclusive prefix of the blocks' local counts
-  if (threadIdx.x == 0) {
-    int run = 0;
-    for (int b = 0; b < s.nblk; ++b) {
-      const int c = s.blk_nloc[b];
-      s.blk_nloc[b] = run;
-      run += c;
+  // exclusive prefix of the blocks' local counts (at most kPermThreads blocks per pass)
+  {
+    int carry = 0;
+    for (int b0 = 0; b0 < s.nblk; b0 += kPermThreads) {
+      const int b = b0 + threadIdx.x;
+      const int c = b < s.nblk ? s.blk_nloc[b] : 0;
+      int tot = 0;
+      const int ex = block_excl_scan(c, s_warp, &tot);
+      if (b < s.nblk) s.blk_nloc[b] = carry + ex;
+      carry += tot;
     }
   }
   if (p.sorted_expert_ids && p.alignment > 0) {
