@@ -280,19 +280,27 @@ using R1 = RowsCfg<1, 32, 2>;          // tokens on M: gate+up halves -> SwiGLU 
 using R2 = RowsCfg<0, 8, 4>;           // tokens on M: plain -> bf16 (K <= 1024)
 using P1 = PairCfg<32, 2>;             // CTA pairs, 256 tokens x 128 channels: gate+up -> SwiGLU -> e4m3 (K <= 4096)
 
+// The grouped GEMM claims its tiles after the first round from the counter the tile-list
+// builder zeroed (ntiles[1]) when a tile has at least 4 K steps; shorter tiles keep the static
+// round robin, where a claim per tile costs more than the balance it buys.
+int* claim_counter(int* ntiles, int nkb) { return nkb >= 4 ? ntiles + 1 : nullptr; }
+
 template <class C>
 int launch_gemm(const GemmArgs& a, cudaStream_t st, int num_sms) {
   static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!configured[dev]) {
-    if (int rc = cuda_check(cudaFuncSetAttribute(k_grouped_gemm<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 C::SMEM_BYTES),
-                            "cudaFuncSetAttribute(grouped_gemm)"))
-      return rc;
+    for (auto fn : {k_grouped_gemm<C, false>, k_grouped_gemm<C, true>})
+      if (int rc = cuda_check(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES),
+                              "cudaFuncSetAttribute(grouped_gemm)"))
+        return rc;
     configured[dev] = true;
   }
-  launch_k(k_grouped_gemm<C>, dim3(num_sms), dim3(C::THREADS), C::SMEM_BYTES, st, a);
+  if (a.tile_next)
+    launch_k(k_grouped_gemm<C, true>, dim3(num_sms), dim3(C::THREADS), C::SMEM_BYTES, st, a);
+  else
+    launch_k(k_grouped_gemm<C, false>, dim3(num_sms), dim3(C::THREADS), C::SMEM_BYTES, st, a);
   return cuda_check(cudaGetLastError(), "launch grouped_gemm");
 }
 
@@ -675,7 +683,7 @@ int msv_fp8_quant_128(const void* x, int64_t ldx, int M, int K, const int32_t* r
 size_t msv_ragged_gemm_workspace_size(int M, int N) {
   Carver c{nullptr};
   c.take<int4>(tile_cap(M, M, 32, N / 128));
-  c.take<int>(1);
+  c.take<int>(2);
   return c.off + 256;
 }
 
@@ -695,7 +703,7 @@ int msv_ragged_moe_gemm_fp8(const uint8_t* a, const float* a_scale, int M, int K
   const size_t cap = tile_cap(M, M, 32, nb);
   Carver c{static_cast<uint8_t*>(workspace)};
   int4* tiles = c.take<int4>(cap);
-  int* ntiles = c.take<int>(1);
+  int* ntiles = c.take<int>(2);  // tile count, claim counter
   launch_k(k_tiles_from_runs, dim3(1), dim3(1024), 0, stream, m_indices, M, bn, nb, tiles, ntiles, (int)cap);
   if (int rc = cuda_check(cudaGetLastError(), "launch tiles_from_runs")) return rc;
   GemmArgs g{};
@@ -712,6 +720,7 @@ int msv_ragged_moe_gemm_fp8(const uint8_t* a, const float* a_scale, int M, int K
   g.as_kb = 1;
   g.tiles = tiles;
   g.num_tiles = ntiles;
+  g.tile_next = claim_counter(ntiles, K / 128);
   g.num_kb = K / 128;
   g.out = out;
   g.out_ld = N;
@@ -762,6 +771,7 @@ int msv_ragged_moe_gemm_fp8_noalloc(const uint8_t* a, const float* a_scale, int 
   g.as_kb = 1;
   g.tiles = tiles;
   g.num_tiles = ntiles;
+  g.tile_next = claim_counter(ntiles, K / 128);
   g.num_kb = K / 128;
   g.out = out;
   g.out_ld = N;
@@ -772,7 +782,7 @@ int msv_ragged_moe_gemm_fp8_noalloc(const uint8_t* a, const float* a_scale, int 
 size_t msv_gemm_fp8_workspace_size(int M, int N) {
   Carver c{nullptr};
   c.take<int4>(tile_cap(1, M, 32, N / 128));
-  c.take<int>(1);
+  c.take<int>(2);
   return c.off + 256;
 }
 
@@ -790,7 +800,7 @@ int msv_gemm_fp8_nt_groupwise(const uint8_t* a, const float* a_scale, int M, int
   const int bn = variant_bn(small), nb = N / 128;
   Carver c{static_cast<uint8_t*>(workspace)};
   int4* tiles = c.take<int4>(tile_cap(1, M, 32, nb));
-  int* ntiles = c.take<int>(1);
+  int* ntiles = c.take<int>(2);  // tile count, claim counter
   launch_k(k_tiles_dense, dim3(64), dim3(256), 0, stream, M, bn, nb, tiles, ntiles);
   if (int rc = cuda_check(cudaGetLastError(), "launch tiles_dense")) return rc;
   GemmArgs g{};
@@ -806,6 +816,7 @@ int msv_gemm_fp8_nt_groupwise(const uint8_t* a, const float* a_scale, int M, int
   g.as_kb = 1;
   g.tiles = tiles;
   g.num_tiles = ntiles;
+  g.tile_next = claim_counter(ntiles, K / 128);
   g.num_kb = K / 128;
   g.out = out;
   g.out_ld = N;
@@ -888,9 +899,9 @@ size_t carve_layer(const LayerPlan& L, uint8_t* base, LayerWs* w) {
   w->slot_row = c.take<int32_t>(L.P);
   w->row_token = c.take<int32_t>(L.P);
   w->tiles1 = c.take<int4>(L.cap1);
-  w->ntiles1 = c.take<int>(1);
+  w->ntiles1 = c.take<int>(2);  // tile count, claim counter
   w->tiles2 = c.take<int4>(L.cap2);
-  w->ntiles2 = c.take<int>(1);
+  w->ntiles2 = c.take<int>(2);
   w->xq = c.take<uint8_t>((size_t)L.rows * L.H);
   w->xs = c.take<float>((size_t)L.srows * (L.H / 128));
   w->aq = c.take<uint8_t>((size_t)L.rows * L.I);
@@ -1134,6 +1145,7 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
     g1.as_kb = L.srows;
     g1.tiles = w.tiles1;
     g1.num_tiles = w.ntiles1;
+    g1.tile_next = claim_counter(w.ntiles1, nkb1);
     g1.num_kb = nkb1;
     g1.out = w.aq;
     g1.out_ld = L.I;
@@ -1198,6 +1210,7 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
     g2.as_kb = L.srows;
     g2.tiles = w.tiles2;
     g2.num_tiles = w.ntiles2;
+    g2.tile_next = claim_counter(w.ntiles2, nkb2);
     g2.num_kb = nkb2;
     g2.out = w.down;
     g2.out_ld = L.H;

@@ -30,6 +30,15 @@
 //               TMEM buffer back as soon as the last load landed, then acc += partial * scale
 //               with paired fp32 FMAs.  At tile end: bf16 out (EPI 0), or SwiGLU + per-128
 //               e4m3 requant (EPI 1: acc 0 = gate rows, acc 1 = up rows of the same channels).
+// Tile order: CTA b starts with tile b; every later tile is claimed from a global counter
+// (GemmArgs::tile_next, zeroed by the tile-list builder) when the producer starts issuing the
+// loads of its current tile.  SMs do not stream at the same rate (measured per CTA: 19 to
+// 28 us for the same 1 MB tile), so a static round robin left the last ~20 % of a launch on a
+// shrinking set of slow SMs.  Tiles of fewer than 4 K steps keep the static order (null
+// tile_next): there a claim per tile costs more than the imbalance it removes.  Either way the
+// producer alone reads the tile list, one tile ahead, and hands each descriptor to the other
+// roles through a shared-memory ring: a global load costs about a microsecond under load, as
+// long as a whole one-K-step tile, and every role used to pay it per tile.
 // Every wait is bounded (common.cuh); on timeout the CTA drains its copies and MMAs, frees
 // TMEM and raises MSV_ERR_TIMEOUT in the error word.
 #pragma once
@@ -48,6 +57,8 @@ struct GemmArgs {
   int64_t as_row, as_kb;
   const int4* tiles;      // {row0, rows, set<<24 | expert, n-block}
   const int* num_tiles;
+  int* tile_next;         // claim counter of the tiles after the first round (0 at launch), or
+                          // null: static round robin
   int num_kb;
   void* out;              // EPI 0: bf16 [rows, out_ld]; EPI 1: e4m3 [rows, out_ld]
   int64_t out_ld;
@@ -71,10 +82,12 @@ struct GemmCfg {
   static constexpr int THREADS = 128 + 128 * NWG;
   static constexpr int NISSUE = 2;
   static constexpr int NSLOT = 8;                       // scale-slot ring depth (K steps)
+  static constexpr int TRING = 16;                      // tile-descriptor ring depth (tiles the producer may lead by)
+  static constexpr int NCONS = NISSUE + 1 + 4 * NWG;    // warps that read each descriptor
   static constexpr int RAW_FLOATS = BN + 4;             // per slot: a_scale of the chunk's rows, w_scale per acc
   static constexpr int SCL_FLOATS = NACC * BN;          // per slot: combined scales
   static constexpr int RED_BYTES = EPI == 1 ? NWG * 4 * CW * 4 : 0;
-  static constexpr int TAIL_BYTES = NSLOT * (RAW_FLOATS + SCL_FLOATS) * 4 + RED_BYTES + 128 * 8 + 64;
+  static constexpr int TAIL_BYTES = NSLOT * (RAW_FLOATS + SCL_FLOATS) * 4 + RED_BYTES + 128 * 8 + TRING * 16 + 64;
   static constexpr int SMEM_LIMIT = 232448 - 1024;  // 227 KB opt-in, minus alignment slack
   static constexpr int NSTAGE_RAW = (SMEM_LIMIT - TAIL_BYTES) / STAGE_BYTES;
   static constexpr int NSTAGE = NSTAGE_RAW > 12 ? 12 : NSTAGE_RAW;
@@ -82,8 +95,9 @@ struct GemmCfg {
   static constexpr int OFF_SCL = OFF_RAW + NSLOT * RAW_FLOATS * 4;
   static constexpr int OFF_RED = OFF_SCL + NSLOT * SCL_FLOATS * 4;
   static constexpr int OFF_BAR = (OFF_RED + RED_BYTES + 7) & ~7;
-  static constexpr int NBARS = 2 * NSTAGE + 2 * NBUF + NISSUE + NWG + 3 * NSLOT;
-  static constexpr int OFF_MISC = OFF_BAR + NBARS * 8;
+  static constexpr int NBARS = 2 * NSTAGE + 2 * NBUF + NISSUE + NWG + 3 * NSLOT + 2 * TRING;
+  static constexpr int OFF_TILE = (OFF_BAR + NBARS * 8 + 15) & ~15;
+  static constexpr int OFF_MISC = OFF_TILE + TRING * 16;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   static_assert(CW % 32 == 0, "column slice must be whole 32-column TMEM loads");
   static_assert(NBUF >= 2, "need at least double-buffered TMEM partials");
@@ -123,7 +137,9 @@ MSV_DEVICE void fma2(float& a0, float& a1, float p0, float p1, float s0, float s
   asm("mov.b64 {%0, %1}, %2;" : "=f"(a0), "=f"(a1) : "l"(d));
 }
 
-template <class C>
+// CLAIM: tiles after the first round come from args.tile_next (false: static round robin).
+// The two orders are separate instantiations so that neither carries the other's code.
+template <class C, bool CLAIM>
 __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_constant__ GemmArgs args) {
   constexpr int BN = C::BN, NACC = C::NACC, NSTAGE = C::NSTAGE, NBUF = C::NBUF, CW = C::CW, NSLOT = C::NSLOT;
   extern __shared__ uint8_t smem_raw[];
@@ -140,6 +156,9 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
   uint64_t* sready = epib + C::NWG;      // raw scales landed (one cp.async arrival per producer lane)
   uint64_t* cready = sready + NSLOT;     // combined scales written by the scale warp
   uint64_t* sfree = cready + NSLOT;      // slot consumed (one arrival per epilogue warp)
+  uint64_t* tfull = sfree + NSLOT;       // tile descriptor published (producer)
+  uint64_t* tfree = tfull + C::TRING;    // tile descriptor read (every consumer warp)
+  int4* s_tile = reinterpret_cast<int4*>(smem + C::OFF_TILE);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
 
@@ -160,6 +179,10 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
       mbar_init(&cready[j], 1);
       mbar_init(&sfree[j], 4 * C::NWG);
     }
+    for (int j = 0; j < C::TRING; ++j) {
+      mbar_init(&tfull[j], 1);
+      mbar_init(&tfree[j], C::NCONS);
+    }
     *s_abort = 0;
     fence_mbar_init();
   }
@@ -175,6 +198,17 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
   pdl_wait();
   const int ntiles = *args.num_tiles;
   const int nkb = args.num_kb;
+  constexpr bool dyn = CLAIM;
+  const int4 kEnd = make_int4(-1, 0, 0, 0);  // ring entry after the last tile (row0 < 0)
+  // this CTA's next tile descriptor from the ring (x < 0: none left); false on timeout or abort
+  auto next_tile = [&](Ring<C::TRING>& tr, int4& td) -> bool {
+    if (!mbar_wait(&tfull[tr.i], tr.ph, s_abort)) return false;
+    td = s_tile[tr.i];
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&tfree[tr.i]);
+    tr.next();
+    return true;
+  };
 
   if (warp == 0) {
     // ───────────── TMA producer (lane 0) + raw scale copies (all lanes) ─────────────
@@ -182,8 +216,25 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
     Ring<NSLOT> sl;
     uint32_t issued = 0;
     bool alive = true;
-    for (int tile = blockIdx.x; tile < ntiles && alive; tile += gridDim.x) {
-      const int4 td = args.tiles[tile];
+    Ring<C::TRING> tr;
+    int tile = blockIdx.x;
+    int4 td = tile < ntiles ? args.tiles[tile] : kEnd;
+    for (;;) {
+      if (!mbar_wait(&tfree[tr.i], tr.ph ^ 1, s_abort)) break;
+      if (lane == 0) {
+        s_tile[tr.i] = td;
+        mbar_arrive(&tfull[tr.i]);
+      }
+      tr.next();
+      if (td.x < 0) break;
+      // the next tile, claimed or known now; its descriptor is loaded at once in the static
+      // order, and two K steps into this tile (the claim has returned by then) when claimed,
+      // so both round trips overlap this tile's loads
+      int nt = tile + (int)gridDim.x;
+      if (dyn && lane == 0) nt = atomicAdd(args.tile_next, 1) + (int)gridDim.x;
+      int4 ntd = kEnd;
+      if (!dyn && nt < ntiles) ntd = args.tiles[nt];
+      const int kb_fetch = dyn ? min(2, nkb - 1) : -1;
       const int set = td.z >> 24, e = td.z & 0xFFFFFF;
       const int nr = td.y;
       // EPI 0 with NACC accumulators: a tile covers NACC consecutive 128-row weight blocks of one
@@ -220,7 +271,14 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
         st.next();
         sl.next();
         ++issued;
+        if (kb == kb_fetch) {
+          nt = __shfl_sync(0xffffffffu, nt, 0);
+          if (nt < ntiles) ntd = args.tiles[nt];
+        }
       }
+      if (!alive) break;
+      tile = nt;
+      td = ntd;
     }
     cp_async_wait_all();
     // no copy into this CTA's shared memory may outlive the CTA
@@ -236,8 +294,11 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
     Ring<NBUF> bf;
     uint32_t step = 0;
     bool alive = true;
-    for (int tile = blockIdx.x; tile < ntiles && alive; tile += gridDim.x) {
-      const int nr = args.tiles[tile].y;
+    Ring<C::TRING> tr;
+    for (;;) {
+      int4 td;
+      if (!next_tile(tr, td) || td.x < 0) break;
+      const int nr = td.y;
       int n_eff = (nr + 15) & ~15;
       n_eff = n_eff < 16 ? 16 : (n_eff > BN ? BN : n_eff);
       const uint32_t idesc = umma_idesc_e4m3(128, n_eff);
@@ -266,6 +327,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
         }
         __syncwarp();
       }
+      if (!alive) break;
     }
     // every MMA must have completed before TMEM is released
     if (lane == 0) {
@@ -277,8 +339,11 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
     // ───────────── scale warp: combined scale per column and accumulator, once per K step ─────────────
     Ring<NSLOT> sl;
     bool alive = true;
-    for (int tile = blockIdx.x; tile < ntiles && alive; tile += gridDim.x) {
-      const int nr = args.tiles[tile].y;
+    Ring<C::TRING> tr;
+    for (;;) {
+      int4 td;
+      if (!next_tile(tr, td) || td.x < 0) break;
+      const int nr = td.y;
       for (int kb = 0; kb < nkb; ++kb, sl.next()) {
         if (!mbar_wait(&sready[sl.i], sl.ph, s_abort)) {
           alive = false;
@@ -298,6 +363,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
         __syncwarp();
         if (lane == 0) mbar_arrive(&cready[sl.i]);
       }
+      if (!alive) break;
     }
   } else {
     // ───────────── epilogue warpgroups ─────────────
@@ -316,8 +382,10 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
       ephase ^= 1;
       return ok;
     };
-    for (int tile = blockIdx.x; tile < ntiles && alive; tile += gridDim.x) {
-      const int4 td = args.tiles[tile];
+    Ring<C::TRING> tr;
+    for (;;) {
+      int4 td;
+      if (!next_tile(tr, td) || td.x < 0) break;
       const int nr = td.y;
       int n_eff = (nr + 15) & ~15;
       n_eff = n_eff < 16 ? 16 : (n_eff > BN ? BN : n_eff);

@@ -463,7 +463,8 @@ struct PermuteArgs {
   int32_t* num_local;
   int32_t* row_token;  // [T*k] token of each sorted row (internal)
   int32_t* slot_row;   // [T*k] sorted row of each slot, -1 when not local (internal)
-  // grouped-GEMM tile lists (internal; nullptr to skip)
+  // grouped-GEMM tile lists (internal; nullptr to skip).  ntiles* point at two ints: the tile
+  // count and the GEMM's tile-claim counter, which the builder zeroes.
   int4* tiles1;
   int* ntiles1;
   int bn1, nb1;
@@ -531,7 +532,10 @@ MSV_DEVICE void build_tiles(const PermuteArgs& p, const int* counts, const int* 
   int total = 0;
   const int base_mine = block_excl_scan(nch * nb, s_warp, &total);
   if (tid < E) info[tid] = make_int4(nsh + base_mine, offsets[tid], c_mine, nch | (cs << 16));
-  if (tid == 0) *ntiles = nsh + total;
+  if (tid == 0) {
+    ntiles[0] = nsh + total;
+    ntiles[1] = 0;  // the GEMM's tile-claim counter
+  }
   __syncthreads();
   // shared-expert tiles
   for (int i = tid; i < nsh; i += kPermThreads) {
@@ -884,7 +888,10 @@ __global__ void __launch_bounds__(1024) k_tiles_from_runs(const int32_t* __restr
     if (threadIdx.x == 1023) s_base = pos + nt;
     __syncthreads();
   }
-  if (threadIdx.x == 0) *ntiles = min(s_base, cap);
+  if (threadIdx.x == 0) {
+    ntiles[0] = min(s_base, cap);
+    ntiles[1] = 0;  // the GEMM's tile-claim counter
+  }
   pdl_trigger();
 }
 
@@ -902,7 +909,10 @@ __global__ void k_tiles_dense(int M, int bn, int nb, int4* __restrict__ tiles, i
     const int r0 = ch * cs;
     tiles[i] = make_int4(r0, max(0, min(cs, M - r0)), 0, nbi);
   }
-  if (blockIdx.x == 0 && threadIdx.x == 0) *ntiles = n;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    ntiles[0] = n;
+    ntiles[1] = 0;  // the GEMM's tile-claim counter
+  }
   pdl_trigger();
 }
 }  // namespace msv
