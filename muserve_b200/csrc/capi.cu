@@ -1019,9 +1019,10 @@ int moe_forward_impl(const msv_moe_shape* s, const msv_moe_weights* W, const voi
     if (int rc = cuda_check(cudaFuncSetAttribute(k_dispatch_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dsm),
                             "cudaFuncSetAttribute(dispatch_quant)"))
       return rc;
-    const int per_cta = kDqMaxSlots / L.k;  // tokens a CTA may take
-    int g = L.T < d->num_sms ? L.T : d->num_sms;
-    const int need = (L.T + per_cta - 1) / per_cta;
+    // CTAs 0 and 1 build the tile lists and take no tokens; the others take at most per_cta
+    const int per_cta = kDqMaxSlots / L.k;
+    int g = L.T + 2 < d->num_sms ? L.T + 2 : d->num_sms;
+    const int need = (L.T + per_cta - 1) / per_cta + 2;
     g = g > need ? g : need;
     launch_k(k_dispatch_quant, dim3(g), dim3(kDqThreads), dsm, stream, p, q);
     if (int rc = cuda_check(cudaGetLastError(), "launch dispatch_quant")) return rc;

@@ -7,12 +7,14 @@
 // whole routing (at most 8192 slot ids, read once into shared memory) into per-warp expert
 // histograms and their prefix, which gives the stable sorted row of any slot:
 //   row(f) = offset[e] + (slots of expert e in earlier warp chunks) + (earlier slots of e in f's chunk)
-// exactly the order of argsort(local ids, stable).  CTA b then takes tokens b, b + G, ...: it
-// places their k slots, quantises each token's row once and writes the e4m3 row and its scales
-// to every sorted row that reads it (its local slots and its shared-expert row), and computes the
-// shared-expert gate.  CTA 0 also writes the per-expert counts and the gate_up GEMM's tile list,
-// CTA 1 (CTA 0 when G == 1) the down GEMM's.  The recount is redundant across CTAs but runs in
-// parallel; the tile lists and the token rows no longer wait for each other.
+// exactly the order of argsort(local ids, stable).  CTA 0 writes the per-expert counts and the
+// gate_up GEMM's tile list, CTA 1 (CTA 0 when G == 1) the down GEMM's; with G > 2 those two take
+// no tokens, and CTA 2 + j takes tokens j, j + (G - 2), ...: it places their k slots, quantises
+// each token's row once and writes the e4m3 row and its scales to every sorted row that reads it
+// (its local slots and its shared-expert row), and computes the shared-expert gate.  The first
+// two tokens' activations are loaded before the recount, which hides their load latency.  The
+// recount is redundant across CTAs but runs in parallel; the tile lists (a few microseconds in
+// one CTA) and the token rows no longer wait for each other.
 #pragma once
 #include "quant_combine.cuh"
 #include "route.cuh"
@@ -36,6 +38,21 @@ __global__ void __launch_bounds__(kDqThreads) k_dispatch_quant(PermuteArgs p, Sc
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int E = p.e_local;
   const int P = p.T * p.k;
+  // this CTA's tokens: tq, tq + Gq, ... (none for the tile-list CTAs 0 and 1 when G > 2)
+  const int G = gridDim.x;
+  const int tb = G > 2 ? 2 : 0;
+  const int Gq = G - tb;
+  const int tq = (int)blockIdx.x - tb;
+  const int ntok = (tq >= 0 && tq < p.T) ? (p.T - tq + Gq - 1) / Gq : 0;
+  // the first pass of the first two tokens (channels c0..c0+3) and of the gate weight: loaded
+  // now, used after the recount
+  const int c0 = threadIdx.x * 4;
+  uint2 xpre0 = make_uint2(0u, 0u), xpre1 = make_uint2(0u, 0u), wpre = make_uint2(0u, 0u);
+  if (c0 < q.K) {
+    if (ntok > 0) xpre0 = *reinterpret_cast<const uint2*>(q.x + (int64_t)tq * q.ldx + c0);
+    if (ntok > 1) xpre1 = *reinterpret_cast<const uint2*>(q.x + (int64_t)(tq + Gq) * q.ldx + c0);
+    if (q.gate_w) wpre = *reinterpret_cast<const uint2*>(q.gate_w + c0);
+  }
   // the per-warp histograms first: the tile builder reuses them as 16-byte int4 records
   int* hist = dq_smem;                     // [kPermWarps][E]: per-warp counts, then bases
   int* counts = hist + kPermWarps * E;     // [E]
@@ -88,11 +105,9 @@ __global__ void __launch_bounds__(kDqThreads) k_dispatch_quant(PermuteArgs p, Sc
     if (blockIdx.x == 0 && p.expert_counts) p.expert_counts[e] = counts[e];
   }
   __syncthreads();
-  // 2. this CTA's tokens (blockIdx.x + i G): sorted rows of their slots, one warp per slot
-  const int G = gridDim.x;
-  const int ntok = ((int)blockIdx.x < p.T) ? (p.T - (int)blockIdx.x + G - 1) / G : 0;
+  // 2. this CTA's tokens: sorted rows of their slots, one warp per slot
   for (int s = warp; s < ntok * p.k; s += kDqThreads / 32) {
-    const int t = (int)blockIdx.x + (s / p.k) * G;
+    const int t = tq + (s / p.k) * Gq;
     const int f = t * p.k + s % p.k;
     const int le = le_of[f];
     int row = -1;
@@ -117,11 +132,14 @@ __global__ void __launch_bounds__(kDqThreads) k_dispatch_quant(PermuteArgs p, Sc
   // 4. quantise each token once and write the e4m3 row and its scales to every row that reads
   // it: 4 channels per thread and pass, so a 128-channel block is one warp
   for (int i = 0; i < ntok; ++i) {
-    const int t = (int)blockIdx.x + i * G;
+    const int t = tq + i * Gq;
     const __nv_bfloat16* __restrict__ xr = q.x + (int64_t)t * q.ldx;
     float dot = 0.f;
-    for (int c = threadIdx.x * 4; c < q.K; c += kDqThreads * 4) {
-      const uint2 raw = *reinterpret_cast<const uint2*>(xr + c);
+    for (int c = c0; c < q.K; c += kDqThreads * 4) {
+      uint2 raw;
+      if (c == c0 && i == 0) raw = xpre0;
+      else if (c == c0 && i == 1) raw = xpre1;
+      else raw = *reinterpret_cast<const uint2*>(xr + c);
       float f[4];
       f[0] = bf16_bits_to_f32(raw.x, 0);
       f[1] = bf16_bits_to_f32(raw.x, 1);
@@ -129,7 +147,7 @@ __global__ void __launch_bounds__(kDqThreads) k_dispatch_quant(PermuteArgs p, Sc
       f[3] = bf16_bits_to_f32(raw.y, 1);
       float am = nanmax(nanmax(fabsf(f[0]), fabsf(f[1])), nanmax(fabsf(f[2]), fabsf(f[3])));
       if (q.gate_w) {
-        const uint2 wraw = *reinterpret_cast<const uint2*>(q.gate_w + c);
+        const uint2 wraw = c == c0 ? wpre : *reinterpret_cast<const uint2*>(q.gate_w + c);
         dot = fmaf(f[0], bf16_bits_to_f32(wraw.x, 0), dot);
         dot = fmaf(f[1], bf16_bits_to_f32(wraw.x, 1), dot);
         dot = fmaf(f[2], bf16_bits_to_f32(wraw.y, 0), dot);
