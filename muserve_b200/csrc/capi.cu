@@ -274,7 +274,8 @@ int tensor_map_f32(CUtensorMap* out, const void* base, uint64_t rows, uint64_t c
 
 using G1Small = GemmCfg<32, 2, 1, 1>;   // gate+up -> SwiGLU -> e4m3, <= 32 rows per chunk
 using G2Small = GemmCfg<32, 1, 0, 1>;   // plain -> bf16, <= 32 rows per chunk
-using G2Pair = GemmCfg<32, 2, 0, 1>;    // plain -> bf16, two 128-row blocks per tile (32 KB of weights per stage)
+using G2Pair = GemmCfg<32, 2, 0, 2>;    // plain -> bf16, two 128-row blocks per tile (32 KB of weights per stage),
+                                        // one epilogue warpgroup per block
 using G2Large = GemmCfg<192, 1, 0, 3>;  // plain -> bf16, <= 192 rows per chunk
 using R1 = RowsCfg<1, 32, 2>;          // tokens on M: gate+up halves -> SwiGLU -> e4m3 (K <= 4096)
 using R2 = RowsCfg<0, 8, 4>;           // tokens on M: plain -> bf16 (K <= 1024)

@@ -28,7 +28,10 @@
 //               column of the tile, computed once into shared memory.
 //   warps 4..   epilogue warpgroups: per K step, tcgen05.ld 32 columns at a time, hand the
 //               TMEM buffer back as soon as the last load landed, then acc += partial * scale
-//               with paired fp32 FMAs.  At tile end: bf16 out (EPI 0), or SwiGLU + per-128
+//               with paired fp32 FMAs.  Each warpgroup takes a column slice of every
+//               accumulator, or (plain bf16 output, one warpgroup per accumulator) all columns
+//               of its own accumulator: tiles of one K step are epilogue-bound, and this halves
+//               the work a warpgroup does per tile.  At tile end: bf16 out (EPI 0), or SwiGLU + per-128
 //               e4m3 requant (EPI 1: acc 0 = gate rows, acc 1 = up rows of the same channels).
 // Tile order: CTA b starts with tile b; every later tile is claimed from a global counter
 // (GemmArgs::tile_next, zeroed by the tile-list builder) when the producer starts issuing the
@@ -78,7 +81,11 @@ struct GemmCfg {
   static constexpr int COLS_USED = NBUF * NACC * BN;
   static constexpr int TMEM_COLS = COLS_USED <= 32 ? 32 : COLS_USED <= 64 ? 64 : COLS_USED <= 128 ? 128
                                    : COLS_USED <= 256 ? 256 : 512;
-  static constexpr int CW = BN / NWG;
+  // EPI 0 with one warpgroup per accumulator (NWG == NACC): each warpgroup promotes all BN
+  // columns of its own accumulator; otherwise each takes a BN / NWG column slice of every one
+  static constexpr bool ASPLIT = EPI == 0 && NACC > 1 && NWG == NACC;
+  static constexpr int NA = ASPLIT ? 1 : NACC;  // accumulators per epilogue thread
+  static constexpr int CW = ASPLIT ? BN : BN / NWG;
   static constexpr int THREADS = 128 + 128 * NWG;
   static constexpr int NISSUE = 2;
   static constexpr int NSLOT = 8;                       // scale-slot ring depth (K steps)
@@ -389,12 +396,16 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
       const int nr = td.y;
       int n_eff = (nr + 15) & ~15;
       n_eff = n_eff < 16 ? 16 : (n_eff > BN ? BN : n_eff);
-      // 32-column groups of this warpgroup's slice that hold real columns
-      const int span = n_eff - wg * CW;
+      // this warpgroup's accumulators [a0, a0 + NA) and columns [cb, cb + CW); the 32-column
+      // groups of them that hold real columns
+      constexpr int NA = C::NA;
+      const int a0 = C::ASPLIT ? wg : 0;
+      const int cb = C::ASPLIT ? 0 : wg * CW;
+      const int span = n_eff - cb;
       const int ngroups = span <= 0 ? 0 : (span >= CW ? CW / 32 : (span + 31) / 32);
-      float acc[NACC][CW];
+      float acc[NA][CW];
 #pragma unroll
-      for (int a = 0; a < NACC; ++a)
+      for (int a = 0; a < NA; ++a)
 #pragma unroll
         for (int c = 0; c < CW; ++c) acc[a][c] = 0.f;
       for (int kb = 0; kb < nkb; ++kb, bf.next(), sl.next()) {
@@ -410,17 +421,18 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
           if (lane == 0) mbar_arrive(&acce[bf.i]);
         }
 #pragma unroll
-        for (int a = 0; a < NACC; ++a) {
+        for (int aa = 0; aa < NA; ++aa) {
+          const int a = a0 + aa;
 #pragma unroll
           for (int g = 0; g < CW / 32; ++g) {
-            const int col = wg * CW + g * 32;
+            const int col = cb + g * 32;
             if (g < ngroups) {
               float pv[32];
               const uint32_t ta = tmem + tlane + (uint32_t)((bf.i * NACC + a) * BN + col);
               if (col + 32 <= n_eff) tmem_ld32(ta, pv);
               else tmem_ld16p(ta, pv);
               tmem_ld_wait();
-              if (a == NACC - 1 && g == ngroups - 1) {  // last load of this step: buffer back to the MMA warps
+              if (aa == NA - 1 && g == ngroups - 1) {  // last load of this step: buffer back to the MMA warps
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&acce[bf.i]);
@@ -429,7 +441,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
 #pragma unroll
               for (int i4 = 0; i4 < 8; ++i4) {
                 const float4 s4 = s4p[i4];
-                float* ac = &acc[a][g * 32 + i4 * 4];
+                float* ac = &acc[aa][g * 32 + i4 * 4];
                 fma2(ac[0], ac[1], pv[i4 * 4 + 0], pv[i4 * 4 + 1], s4.x, s4.y);
                 fma2(ac[2], ac[3], pv[i4 * 4 + 2], pv[i4 * 4 + 3], s4.z, s4.w);
               }
@@ -445,13 +457,13 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
       if constexpr (C::EPI == 0) {
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
 #pragma unroll
-        for (int a = 0; a < NACC; ++a) {
-          const int col = (td.w * NACC + a) * 128 + lrow;
+        for (int aa = 0; aa < NA; ++aa) {
+          const int col = (td.w * NACC + a0 + aa) * 128 + lrow;
 #pragma unroll
           for (int c = 0; c < CW; ++c) {
-            const int t = wg * CW + c;
+            const int t = cb + c;
             if (t >= nr) break;
-            out[(row0 + t) * args.out_ld + col] = __float2bfloat16_rn(acc[a][c]);
+            out[(row0 + t) * args.out_ld + col] = __float2bfloat16_rn(acc[aa][c]);
           }
         }
       } else {
@@ -462,7 +474,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
         for (int c = 0; c < CW; ++c) {
           if (wg * CW + c >= nr) break;  // warp-uniform
           const float g = bf16_round(acc[0][c]);
-          const float u = bf16_round(acc[NACC - 1][c]);
+          const float u = bf16_round(acc[NA - 1][c]);
           const float sg = bf16_round(__fdiv_rn(g, 1.0f + expf(-g)));
           const float av = bf16_round(sg * u);
           acc[0][c] = av;
