@@ -429,7 +429,9 @@ def roofline(r, tokens, *, prefill):
     return roof, dom
 
 
-def layer_summary(r, tokens, tp, comm, nccl_allreduce):
+def layer_summary(r, tokens, tp, comm, nccl_allreduce, combine_alone_ms=None):
+    """``combine_alone_ms``: the plain combine's stage time of the same batch on one GPU; with the
+    fused combine + all-reduce, the all-reduce's own cost is the fused stage minus it."""
     hbm, _, _ = peaks()
     inter, shared, ms_step = r["inter"], r["shared"], r["ms_step"]
     gbs = layer_bytes(r["n_touched"], inter, shared, tokens) / (ms_step / 1e3) / 1e9
@@ -442,7 +444,14 @@ def layer_summary(r, tokens, tp, comm, nccl_allreduce):
             "allreduce_ms": r["ar_ms"] if comm is None else None,
             "allreduce_share": (r["ar_ms"] / ms_step if tp > 1 else 0.0) if comm is None else None,
             "combine_allreduce_ms": r["stage_ms"]["combine"] if comm is not None else None,
-            "combine_allreduce_share": r["stage_ms"]["combine"] / ms_step if comm is not None else None}
+            "combine_allreduce_share": r["stage_ms"]["combine"] / ms_step if comm is not None else None,
+            "allreduce_added_ms": (r["stage_ms"]["combine"] - combine_alone_ms
+                                   if comm is not None and combine_alone_ms is not None else None),
+            "allreduce_added_share": ((r["stage_ms"]["combine"] - combine_alone_ms) / ms_step
+                                      if comm is not None and combine_alone_ms is not None else None),
+            "allreduce_added_how": ("fused combine + all-reduce stage minus the plain combine of the same "
+                                    "batch on one GPU (same_config_1gpu), over this layer's step"
+                                    if comm is not None and combine_alone_ms is not None else None)}
 
 
 def run_ours(args, world, rank, local):
@@ -523,11 +532,12 @@ def run_ours(args, world, rank, local):
     workload = f"tp{tp}_decode_c3{suffix}"
     res = base_line(args, world, r, tokens, n_exp, tp, workload, prefill=False)
     res.update({"roofline": dict(roof, traffic=traffic_for(workload, dom)),
-                "layer": layer_summary(r, tokens, tp, comm, args.nccl_allreduce), "e2e": r.get("e2e"),
-                "cpu_baseline": None,
+                "layer": layer_summary(r, tokens, tp, comm, args.nccl_allreduce,
+                                       combine_alone_ms=one["stage_ms"]["combine"]),
+                "e2e": r.get("e2e"), "cpu_baseline": None,
                 "same_config_1gpu": {
                     "workload": f"decode_t{tokens}_1gpu{suffix}", "value": one["value"], "unit": "tokens/s",
-                    "ms_per_step": one["ms_step"],
+                    "ms_per_step": one["ms_step"], "combine_ms": one["stage_ms"]["combine"],
                     "how": "the same unsharded layer and 256-token batch on one GPU, timed on every rank's own "
                            "GPU before the TP run (max over ranks)"},
                 "efficiency_same_config": r["value"] / (tp * one["value"]),
