@@ -272,7 +272,8 @@ int tensor_map_f32(CUtensorMap* out, const void* base, uint64_t rows, uint64_t c
 
 // ── grouped GEMM variants ────────────────────────────────────────────────────────────────
 
-using G1Small = GemmCfg<32, 2, 1, 1>;   // gate+up -> SwiGLU -> e4m3, <= 32 rows per chunk
+using G1Small = GemmCfg<32, 2, 1, 2>;   // gate+up -> SwiGLU -> e4m3, <= 32 rows per chunk, two epilogue
+                                        // warpgroups of 16 token columns each
 using G2Small = GemmCfg<32, 1, 0, 1>;   // plain -> bf16, <= 32 rows per chunk
 using G2Pair = GemmCfg<32, 2, 0, 2>;    // plain -> bf16, two 128-row blocks per tile (32 KB of weights per stage),
                                         // one epilogue warpgroup per block

@@ -31,7 +31,9 @@
 //               with paired fp32 FMAs.  Each warpgroup takes a column slice of every
 //               accumulator, or (plain bf16 output, one warpgroup per accumulator) all columns
 //               of its own accumulator: tiles of one K step are epilogue-bound, and this halves
-//               the work a warpgroup does per tile.  At tile end: bf16 out (EPI 0), or SwiGLU + per-128
+//               the work a warpgroup does per tile.  A 16-column slice loads TMEM 16 columns at a
+//               time (gate_up with two warpgroups: the SwiGLU finish of a 32-token tile, one
+//               chain per column, runs on eight warps instead of four).  At tile end: bf16 out (EPI 0), or SwiGLU + per-128
 //               e4m3 requant (EPI 1: acc 0 = gate rows, acc 1 = up rows of the same channels).
 // Tile order: CTA b starts with tile b; every later tile is claimed from a global counter
 // (GemmArgs::tile_next, zeroed by the tile-list builder) when the producer starts issuing the
@@ -106,7 +108,8 @@ struct GemmCfg {
   static constexpr int OFF_TILE = (OFF_BAR + NBARS * 8 + 15) & ~15;
   static constexpr int OFF_MISC = OFF_TILE + TRING * 16;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
-  static_assert(CW % 32 == 0, "column slice must be whole 32-column TMEM loads");
+  static constexpr int LW = CW < 32 ? CW : 32;  // columns per TMEM load (16 or 32)
+  static_assert(CW % 16 == 0 && CW % LW == 0, "column slice must be whole 16- or 32-column TMEM loads");
   static_assert(NBUF >= 2, "need at least double-buffered TMEM partials");
   static_assert(NSTAGE >= 2, "pipeline too shallow");
   static_assert(NBARS <= 128, "barrier area");
@@ -402,7 +405,8 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
       const int a0 = C::ASPLIT ? wg : 0;
       const int cb = C::ASPLIT ? 0 : wg * CW;
       const int span = n_eff - cb;
-      const int ngroups = span <= 0 ? 0 : (span >= CW ? CW / 32 : (span + 31) / 32);
+      constexpr int LW = C::LW;
+      const int ngroups = span <= 0 ? 0 : (span >= CW ? CW / LW : (span + LW - 1) / LW);
       float acc[NA][CW];
 #pragma unroll
       for (int a = 0; a < NA; ++a)
@@ -424,13 +428,17 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
         for (int aa = 0; aa < NA; ++aa) {
           const int a = a0 + aa;
 #pragma unroll
-          for (int g = 0; g < CW / 32; ++g) {
-            const int col = cb + g * 32;
+          for (int g = 0; g < CW / LW; ++g) {
+            const int col = cb + g * LW;
             if (g < ngroups) {
-              float pv[32];
+              float pv[LW];
               const uint32_t ta = tmem + tlane + (uint32_t)((bf.i * NACC + a) * BN + col);
-              if (col + 32 <= n_eff) tmem_ld32(ta, pv);
-              else tmem_ld16p(ta, pv);
+              if constexpr (LW == 32) {
+                if (col + 32 <= n_eff) tmem_ld32(ta, pv);
+                else tmem_ld16p(ta, pv);
+              } else {
+                tmem_ld16p(ta, pv);
+              }
               tmem_ld_wait();
               if (aa == NA - 1 && g == ngroups - 1) {  // last load of this step: buffer back to the MMA warps
                 tc_fence_before();
@@ -439,9 +447,9 @@ __global__ void __launch_bounds__(C::THREADS, 1) k_grouped_gemm(const __grid_con
               }
               const float4* s4p = reinterpret_cast<const float4*>(sc + a * BN + col);
 #pragma unroll
-              for (int i4 = 0; i4 < 8; ++i4) {
+              for (int i4 = 0; i4 < LW / 4; ++i4) {
                 const float4 s4 = s4p[i4];
-                float* ac = &acc[aa][g * 32 + i4 * 4];
+                float* ac = &acc[aa][g * LW + i4 * 4];
                 fma2(ac[0], ac[1], pv[i4 * 4 + 0], pv[i4 * 4 + 1], s4.x, s4.y);
                 fma2(ac[2], ac[3], pv[i4 * 4 + 2], pv[i4 * 4 + 3], s4.z, s4.w);
               }
