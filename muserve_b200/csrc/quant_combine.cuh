@@ -244,6 +244,8 @@ template <int MODE, class Store>
 MSV_DEVICE void combine_token(const CombineArgs& a, int t, int* s_row, float* s_w, Store&& store, int c_begin = 0,
                               int c_end = -1) {
   if (c_end < 0) c_end = a.H;
+  // the shared-expert gate loads first: its latency overlaps the slot setup below
+  const float gv = (a.add_shared && a.gate_val) ? a.gate_val[t] : 1.0f;
   __syncthreads();  // the previous token's slots are no longer read
   if (threadIdx.x < 32) {
     const int j = threadIdx.x;
@@ -270,7 +272,6 @@ MSV_DEVICE void combine_token(const CombineArgs& a, int t, int* s_row, float* s_
     }
   }
   __syncthreads();
-  const float gv = (a.add_shared && a.gate_val) ? a.gate_val[t] : 1.0f;
   for (int c = c_begin + threadIdx.x * 8; c < c_end; c += blockDim.x * 8) {
     float acc[8];
 #pragma unroll
