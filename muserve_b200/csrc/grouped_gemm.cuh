@@ -9,7 +9,7 @@
 // side and a group's tokens form N (16..BN, multiple of 16), so an expert with 1 token
 // (decode) or 160 tokens (prefill) pays no M padding and each weight tile is streamed from
 // HBM once per token chunk.  A tile = (group, n-block, token chunk); the tile list is built
-// on the device, the kernel is persistent (one CTA per SM, static round robin over tiles).
+// on the device, the kernel is persistent (one CTA per SM; tile order below).
 //
 // The 128x128 fp32 weight scales and per-row x 128 activation scales are arbitrary fp32
 // values, so they cannot be folded into a UE8M0 block-scaled MMA: every 128-wide K block
