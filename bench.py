@@ -212,11 +212,13 @@ def time_layer(args, lib, dev, w, x, *, tokens, n_exp, logits=None, tp=1, comm=N
     for row in evs:  # create the event handles before anything is timed
         for e in row:
             e.record(stream)
-    # Timed steps record only the events around the two GEMMs (indices 3, 4, 5: each recorded
-    # event between kernels costs about 3 us of device time); the other stages are timed in
-    # separate fully instrumented steps after the timed region.  The extra last event of a row
-    # marks the start of the router GEMM when the step routes from the hidden states.
-    GEMM_EV = (3, 4, 5)
+    # Timed steps record only the two events around the gate_up GEMM, the roofline's kernel
+    # (indices 3, 4: each recorded event between kernels costs about 3 us of device time and
+    # stops the next launch from overlapping the previous one); the other stages, the down GEMM
+    # among them, are timed in separate fully instrumented steps after the timed region.  The
+    # extra last event of a row marks the start of the router GEMM when the step routes from
+    # the hidden states.
+    GEMM_EV = (3, 4)
     ev_arrays = [(ctypes.c_void_p * nst)(*[e.cuda_event if j in GEMM_EV else None for j, e in enumerate(row[:nst])])
                  for row in evs]
     n_prof = min(args.steps, 10)
@@ -294,8 +296,8 @@ def time_layer(args, lib, dev, w, x, *, tokens, n_exp, logits=None, tp=1, comm=N
     barrier()
     ms_total = max_over_ranks(t0.elapsed_time(t1))
     _lib.check(lib.msv_check_device_error(sp), "timed region")
-    # the small stages from fully instrumented steps after the timed region (same collectives on
-    # every rank), the GEMMs from the timed steps themselves
+    # the other stages from fully instrumented steps after the timed region (same collectives on
+    # every rank), the gate_up GEMM from the timed steps themselves
     for i in range(n_prof):
         step(i, prof=True)
     torch.cuda.synchronize()
