@@ -26,15 +26,16 @@
 //               every step has its own stage and buffer, so the order they run in is free.
 //   warp 3      scale warp: per K step, combined scale a_scale[row] * w_scale[acc] for every
 //               column of the tile, computed once into shared memory.
-//   warps 4..   epilogue warpgroups: per K step, tcgen05.ld 32 columns at a time, hand the
-//               TMEM buffer back as soon as the last load landed, then acc += partial * scale
-//               with paired fp32 FMAs.  Each warpgroup takes a column slice of every
-//               accumulator, or (plain bf16 output, one warpgroup per accumulator) all columns
-//               of its own accumulator: tiles of one K step are epilogue-bound, and this halves
-//               the work a warpgroup does per tile.  A 16-column slice loads TMEM 16 columns at a
-//               time (gate_up with two warpgroups: the SwiGLU finish of a 32-token tile, one
-//               chain per column, runs on eight warps instead of four).  At tile end: bf16 out (EPI 0), or SwiGLU + per-128
-//               e4m3 requant (EPI 1: acc 0 = gate rows, acc 1 = up rows of the same channels).
+//   warps 4..   epilogue warpgroups: per K step, tcgen05.ld 32 (or 16) columns at a time,
+//               hand the TMEM buffer back as soon as the last load landed, then
+//               acc += partial * scale with paired fp32 FMAs.  Each warpgroup takes a column
+//               slice of every accumulator, or (plain bf16 output, one warpgroup per
+//               accumulator) all columns of its own accumulator: tiles of one K step are
+//               epilogue-bound, and this halves the work a warpgroup does per tile.  A 16-column
+//               slice loads TMEM 16 columns at a time (gate_up with two warpgroups: the SwiGLU
+//               finish of a 32-token tile, one chain per column, runs on eight warps instead of
+//               four).  At tile end: bf16 out (EPI 0), or SwiGLU + per-128 e4m3 requant (EPI 1:
+//               acc 0 = gate rows, acc 1 = up rows of the same channels).
 // Tile order: CTA b starts with tile b; every later tile is claimed from a global counter
 // (GemmArgs::tile_next, zeroed by the tile-list builder) when the producer starts issuing the
 // loads of its current tile.  SMs do not stream at the same rate (measured per CTA: 19 to
@@ -43,7 +44,7 @@
 // tile_next): there a claim per tile costs more than the imbalance it removes.  Either way the
 // producer alone reads the tile list, one tile ahead, and hands each descriptor to the other
 // roles through a shared-memory ring: a global load costs about a microsecond under load, as
-// long as a whole one-K-step tile, and every role used to pay it per tile.
+// long as a whole one-K-step tile, which every role would otherwise pay per tile.
 // Every wait is bounded (common.cuh); on timeout the CTA drains its copies and MMAs, frees
 // TMEM and raises MSV_ERR_TIMEOUT in the error word.
 #pragma once
